@@ -1,0 +1,526 @@
+"""Benchmark of the Block AttnRes operator on B200.
+
+Workload (one "step"): forward + backward of ``block_attn_res_triton`` at
+N=9, B=1, T=4096, D=2048 bf16 with v ~ N(0,1), w ~ N(0,1/D), dout ~ N(0,1)
+(synthetic; the reference uses no dataset). L2 (126 MB) is flushed with a
+384 MiB memset before every timed step, outside that step's CUDA events, and a
+short spin kernel lets the host queue the whole step before it starts, so the
+events see device time only.
+
+Printed: ONE JSON line (rank 0). ``value`` = achieved HBM TB/s of the step's
+algorithmic bytes, (3N+2)*B*T*D*2 per rank, summed over ranks, divided by the
+max-over-ranks mean step time. Extra keys carry the forward-alone latency and
+TB/s, the speed-of-light kernel, per-kernel rooflines, batched queries, the
+CPU baseline, the end-to-end number through the public API with host buffers,
+and the SM clocks sampled (NVML) during the timed region.
+
+``--gpus N`` (under torchrun): each rank runs the same shape on its own token
+shard (weak scaling); the step's only exchange is the fp32 dw all-gather of
+``switchyard.sharding`` (NCCL).
+
+``--impl reference``: the reference's PyTorch eager CPU path (restated in
+``oracle/eager_port.py``; the reference itself cannot run on the GPU box),
+fwd+bwd on a bounded token sample on all host threads; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT / "blackwell-switchyard_b200", ROOT):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import torch  # noqa: E402
+
+METRIC = "fwd & fwd+bwd µs and achieved HBM TB/s (% of roofline) at N=9 T=4096 D=2048 bf16"
+REP = (9, 1, 4096, 2048)
+ITEM = 2  # bf16
+FLUSH_BYTES = 384 * 2**20
+FALLBACK_HBM_GBS = 6650.0
+CPU_SAMPLE_T = 256  # tokens per CPU-baseline step (bounded sample of the workload)
+
+
+# ----------------------------------------------------------------------------- setup
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline budget")
+    ap.add_argument("--no-extras", action="store_true", help="skip batched/SoL/e2e extras")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", 0))
+    return rank, world, local
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def alg_bytes(n, b, t, d, itemsize=ITEM):
+    fwd = (n + 1) * b * t * d * itemsize
+    bwd = (2 * n + 1) * b * t * d * itemsize
+    return fwd, bwd, fwd + bwd
+
+
+# ----------------------------------------------------------------------------- clocks
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons via NVML every few ms."""
+
+    REASONS = {
+        "sw_power_cap": 0x4,
+        "hw_slowdown": 0x8,
+        "sync_boost": 0x10,
+        "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, device_index: int, period_s: float = 0.005):
+        self.ok = False
+        self.samples = []
+        self.reasons = set()
+        self.max_mhz = None
+        self.period = period_s
+        self._stop = threading.Event()
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            bus = torch.cuda.get_device_properties(device_index).pci_bus_id
+            try:
+                self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:  # noqa: BLE001
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.nv = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as exc:  # noqa: BLE001
+            self.err = str(exc)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                self.samples.append(mhz)
+                for name, bit in self.REASONS.items():
+                    if mask & bit:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": f"nvml unavailable: {self.err}"}
+        return {
+            "sm_mhz": statistics.median(self.samples) if self.samples else None,
+            "sm_max_mhz": self.max_mhz,
+            "reasons": sorted(self.reasons),
+            "samples": len(self.samples),
+        }
+
+
+# ----------------------------------------------------------------------------- timing
+
+
+def timed_steps(fn, steps, flush, lead_cycles=400_000):
+    """Per-step device times (ms): flush L2, let a spin kernel cover the host's
+    queueing of the step, then bracket only the step with CUDA events on the
+    current stream."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()
+        torch.cuda._sleep(lead_cycles)
+        starts[i].record()
+        fn()
+        ends[i].record()
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+def summarize(ms):
+    ms = sorted(ms)
+    n = len(ms)
+    return {
+        "mean_ms": statistics.fmean(ms),
+        "median_ms": ms[n // 2],
+        "p10_ms": ms[max(0, int(0.1 * n))],
+        "p90_ms": ms[min(n - 1, int(0.9 * n))],
+        "min_ms": ms[0],
+    }
+
+
+# ----------------------------------------------------------------------------- our arm
+
+
+def make_inputs(dev, rank, n, b, t, d, dtype=torch.bfloat16):
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    v = torch.randn(n, b, t, d, device=dev, generator=g, dtype=torch.float32).to(dtype)
+    gw = torch.Generator(device=dev).manual_seed(1)  # the query is shared by all ranks
+    w = (torch.randn(d, device=dev, generator=gw) / math.sqrt(d)).to(dtype)
+    dout = torch.randn(b, t, d, device=dev, generator=g, dtype=torch.float32).to(dtype)
+    return v, w, dout
+
+
+def cpu_baseline(seconds: float):
+    """The reference's eager CPU path (restated in oracle/eager_port.py),
+    fwd+bwd, on a bounded sample of the workload: T=256 of the 4096 tokens."""
+    from oracle.eager_port import fwd_bwd
+
+    n, b, _, d = REP
+    t = CPU_SAMPLE_T
+    gen = torch.Generator().manual_seed(0)
+    v = torch.randn(n, b, t, d, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(d, generator=gen) / math.sqrt(d)).to(torch.bfloat16)
+    g = torch.randn(b, t, d, generator=gen).to(torch.bfloat16)
+    fwd_bwd(v, w, g)
+    times = []
+    t_end = time.perf_counter() + seconds
+    while len(times) < 3 or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        fwd_bwd(v, w, g)
+        times.append(time.perf_counter() - t0)
+    per = statistics.median(times)
+    _, _, tot = alg_bytes(n, b, t, d)
+    return {
+        "value": tot / per / 1e12,
+        "unit": "TB/s",
+        "cores": torch.get_num_threads(),
+        "kind": "port",
+        "sample": f"fwd+bwd of the reference eager path (oracle/eager_port.py) on N={n} B={b} T={t} D={d} bf16 "
+                  f"(T={t} of 4096 tokens), median of {len(times)} runs, {per * 1e3:.1f} ms each",
+        "ms_per_sample": per * 1e3,
+        "cpu_count": os.cpu_count(),
+    }
+
+
+def kernel_times(native, v, w, dout, steps, flush, stream):
+    """Device time of each of our kernels launched alone through the C ABI."""
+    n, b, t, d = v.shape
+    bt = b * t
+    out = torch.empty(b, t, d, device=v.device, dtype=v.dtype)
+    stats = torch.empty(bt, native.stats_stride(n), device=v.device, dtype=torch.float32)
+    dv = torch.empty_like(v)
+    p = native.bwd_partials(n, bt, d, v.dtype)
+    part = torch.empty(p, d, device=v.device, dtype=torch.float32)
+    dw = torch.empty(d, device=v.device, dtype=w.dtype)
+    sol = torch.empty_like(out)
+    res = {}
+    calls = {
+        "fwd": lambda: native.fwd(v, w, out, stats, n, bt, d, 1e-6),
+        "bwd": lambda: native.bwd(v, w, dout, stats, dv, part, n, bt, d, 1e-6),
+        "dw_reduce": lambda: native.dw_reduce(part, dw),
+        "speed_of_light": lambda: native.speed_of_light(v, sol, n, bt, d),
+    }
+    calls["fwd"]()
+    for name, fn in calls.items():
+        for _ in range(3):
+            fn()
+        res[name] = summarize(timed_steps(fn, steps, flush))
+    return res, p
+
+
+def batched_times(v, steps, flush, qs=(1, 4, 8, 16)):
+    from switchyard import block_attn_res_batched
+
+    n, b, t, d = v.shape
+    out = {}
+    gen = torch.Generator(device=v.device).manual_seed(7)
+    for q in qs:
+        queries = (torch.randn(q, d, device=v.device, generator=gen) / math.sqrt(d)).to(v.dtype)
+        with torch.no_grad():
+            fn = lambda: block_attn_res_batched(v, queries)  # noqa: E731
+            for _ in range(3):
+                fn()
+            s = summarize(timed_steps(fn, steps, flush))
+        byts = ((n + q) * b * t * d + q * d) * ITEM
+        flops = (2 + 4 * q) * n * b * t * d
+        s["tbps"] = byts / (s["mean_ms"] * 1e-3) / 1e12
+        s["bytes"] = byts
+        s["flops"] = flops
+        out[f"Q{q}"] = s
+    return out
+
+
+def e2e_times(dev, steps, n, b, t, d, op):
+    """Same step through the public API from pinned host buffers: H2D of v, w
+    and dout, forward + backward, D2H of dw -- all inside the events."""
+    gen = torch.Generator().manual_seed(3)
+    v_h = torch.randn(n, b, t, d, generator=gen).to(torch.bfloat16).pin_memory()
+    w_h = (torch.randn(d, generator=gen) / math.sqrt(d)).to(torch.bfloat16).pin_memory()
+    g_h = torch.randn(b, t, d, generator=gen).to(torch.bfloat16).pin_memory()
+    dw_h = torch.empty(d, dtype=torch.bfloat16).pin_memory()
+
+    def step():
+        v = v_h.to(dev, non_blocking=True).requires_grad_(True)
+        w = w_h.to(dev, non_blocking=True).requires_grad_(True)
+        g = g_h.to(dev, non_blocking=True)
+        op(v, w).backward(g)
+        dw_h.copy_(w.grad, non_blocking=True)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    ms = []
+    for _ in range(steps):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        step()
+        e.record()
+        torch.cuda.synchronize()
+        ms.append(s.elapsed_time(e))
+    h2d = v_h.numel() * 2 + w_h.numel() * 2 + g_h.numel() * 2
+    return summarize(ms), h2d, dw_h.numel() * 2
+
+
+def run_ours(args):
+    import torch.distributed as dist
+
+    from switchyard import _native, block_attn_res_triton, speed_of_light  # noqa: F401
+    from switchyard.sharding import block_attn_res_sharded
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    n, b, t, d = REP
+    v, w, dout = make_inputs(dev, rank, n, b, t, d)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    op = block_attn_res_triton if world == 1 else block_attn_res_sharded
+
+    def step():
+        vv = v.detach().requires_grad_(True)
+        ww = w.detach().requires_grad_(True)
+        op(vv, ww).backward(dout)
+
+    def fwd_only():
+        with torch.no_grad():
+            block_attn_res_triton(v, w)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+        fwd_only()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with sampler:
+        step_ms = timed_steps(step, args.steps, flush)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    fwd_ms = timed_steps(fwd_only, args.steps, flush)
+
+    st_step, st_fwd = summarize(step_ms), summarize(fwd_ms)
+    mean_step, mean_fwd = st_step["mean_ms"], st_fwd["mean_ms"]
+    if world > 1:
+        tt = torch.tensor([mean_step, mean_fwd], device=dev, dtype=torch.float64)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        mean_step, mean_fwd = tt.tolist()
+
+    fwd_b, bwd_b, tot_b = alg_bytes(n, b, t, d)
+    peak, peak_kind = load_peaks()
+    result = None
+    if rank == 0:
+        kt, p_rows = kernel_times(_native, v, w, dout, args.steps, flush, None)
+        value = world * tot_b / (mean_step * 1e-3) / 1e12
+        bwd_ach = bwd_b / (kt["bwd"]["mean_ms"] * 1e-3) / 1e9
+        fwd_ach = fwd_b / (kt["fwd"]["mean_ms"] * 1e-3) / 1e9
+        sol_ach = fwd_b / (kt["speed_of_light"]["mean_ms"] * 1e-3) / 1e9
+        traffic = read_traffic()
+        result = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "TB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": mean_step,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "bf16",
+            "data": "synthetic: v~N(0,1), w~N(0,1/D), dout~N(0,1), seeds 1000+rank / 1 / 1000+rank",
+            "config": {
+                "workload": "Block AttnRes forward+backward (block_attn_res_triton, autograd) per step",
+                "N": n, "B": b, "T": t, "D": d, "tokens_per_rank": b * t,
+                "l2": "flushed (384 MiB memset) before every timed step, outside its events",
+                "parallelism": f"token-axis shards x{world}" if world > 1 else "single GPU",
+            },
+            "fwd_us": mean_fwd * 1e3,
+            "fwd_bwd_us": mean_step * 1e3,
+            "fwd_tbps": world * fwd_b / (mean_fwd * 1e-3) / 1e12,
+            "fwd_frac_of_peak": (fwd_b / (mean_fwd * 1e-3) / 1e9) / peak,
+            "fwd_bwd_frac_of_peak": (tot_b / (mean_step * 1e-3) / 1e9) / peak,
+            "step_stats": st_step,
+            "fwd_stats": st_fwd,
+            "roofline": {
+                "kernel": "tile_bwd_kernel (sy_bwd)",
+                "bound": "hbm",
+                "achieved": bwd_ach,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": bwd_ach / peak,
+                "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured" else "fallback",
+                "algorithmic_bytes": bwd_b,
+                "traffic": traffic.get("bwd"),
+            },
+            "roofline_fwd": {
+                "kernel": "tile_fwd_kernel (sy_fwd)",
+                "bound": "hbm",
+                "achieved": fwd_ach,
+                "peak": peak,
+                "unit": "GB/s",
+                "frac": fwd_ach / peak,
+                "algorithmic_bytes": fwd_b,
+                "traffic": traffic.get("fwd"),
+                "speed_of_light_kernel_gbs": sol_ach,
+                "frac_of_speed_of_light": fwd_ach / sol_ach,
+            },
+            "kernels_ms": {k: v_["mean_ms"] for k, v_ in kt.items()},
+            "dw_partial_rows": p_rows,
+            "gpu_launches": 3 * args.steps,
+            "clocks": sampler.summary(),
+        }
+    if not args.no_extras and rank == 0:
+        result["batched"] = batched_times(v, max(20, args.steps // 4), flush)
+        e2e, h2d, d2h = e2e_times(dev, 10, n, b, t, d, block_attn_res_triton)
+        result["e2e"] = {
+            "value": tot_b / (e2e["mean_ms"] * 1e-3) / 1e12,
+            "unit": "TB/s",
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "ms_per_step": e2e["mean_ms"],
+            "api": "switchyard.block_attn_res_triton (autograd) from pinned host buffers, rank 0",
+        }
+    if rank == 0 and world == 1:
+        result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def read_traffic():
+    """DRAM bytes per launch from the committed ncu summary, if one exists:
+    lines ``traffic_bytes_per_launch <fwd|bwd> <bytes>`` in profiles/*.txt."""
+    out = {}
+    for p in sorted((ROOT / "profiles").glob("*.txt")):
+        for line in p.read_text().splitlines():
+            parts = line.split()
+            if len(parts) == 3 and parts[0] == "traffic_bytes_per_launch":
+                try:
+                    out[parts[1]] = float(parts[2])
+                except ValueError:
+                    pass
+    return out
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from oracle.eager_port import fwd_bwd
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    n, b, _, d = REP
+    t = CPU_SAMPLE_T
+    gen = torch.Generator().manual_seed(0)
+    v = torch.randn(n, b, t, d, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(d, generator=gen) / math.sqrt(d)).to(torch.bfloat16)
+    g = torch.randn(b, t, d, generator=gen).to(torch.bfloat16)
+    for _ in range(max(args.warmup, 1)):
+        fwd_bwd(v, w, g)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        fwd_bwd(v, w, g)
+        times.append(time.perf_counter() - t0)
+    mean = statistics.fmean(times)
+    _, _, tot = alg_bytes(n, b, t, d)
+    value = tot / mean / 1e12
+    sample = (f"reference eager fwd+bwd (oracle/eager_port.py) on N={n} B={b} T={t} D={d} bf16, "
+              f"T={t} of the 4096 tokens per step")
+    print(json.dumps({
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "TB/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": mean * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: v~N(0,1), w~N(0,1/D), dout~N(0,1)",
+        "config": {"workload": "Block AttnRes forward+backward, reference PyTorch eager on CPU",
+                   "N": n, "B": b, "T": t, "D": d, "sampled_from_T": REP[2]},
+        "cpu_baseline": {"value": value, "unit": "TB/s", "cores": torch.get_num_threads(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,121 @@
+"""Build libswitchyard_b200.so (the C-ABI library) in-tree with nvcc.
+
+Every ``.cu`` file in this directory is compiled for sm_100a only, as
+relocatable device code (the device error word is shared across files), in
+parallel, then device-linked into one shared library that lands next to the
+Python package that loads it. The library links the *shared* CUDA runtime, so
+in a process that already imported torch it uses torch's runtime and sees the
+same current device.
+
+Usage: ``python build.py [--force] [--jobs N]``. Rebuilds only when the
+content of a source, header or of this script changed since the last build (a
+hash stamp beside the library; file times are unreliable after copies).
+"""
+
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import hashlib
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+PKG = HERE.parent / "switchyard"
+LIB = PKG / "libswitchyard_b200.so"
+STAMP = PKG / "libswitchyard_b200.stamp"
+INCLUDE = HERE.parent.parent / "include"
+BUILD = HERE.parent / "_build"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+FLAGS = [
+    "-O3",
+    "-std=c++17",
+    "-lineinfo",
+    "-rdc=true",
+    "-Xcompiler",
+    "-fPIC",
+    "-Xcompiler",
+    "-fvisibility=hidden",
+    "--expt-relaxed-constexpr",
+    f"-I{INCLUDE}",
+]
+
+
+def _nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found: the switchyard CUDA library cannot be built")
+
+
+def _sources() -> list[Path]:
+    return sorted(HERE.glob("*.cu"))
+
+
+def _deps() -> list[Path]:
+    return _sources() + sorted(HERE.glob("*.cuh")) + sorted(INCLUDE.glob("*.h")) + [Path(__file__)]
+
+
+def _digest() -> str:
+    h = hashlib.sha256()
+    for p in _deps():
+        h.update(p.name.encode())
+        h.update(p.read_bytes())
+    h.update(" ".join(ARCH + FLAGS).encode())
+    return h.hexdigest()
+
+
+def up_to_date() -> bool:
+    return LIB.exists() and STAMP.exists() and STAMP.read_text().strip() == _digest()
+
+
+def _run(cmd: list[str]) -> tuple[list[str], int, str]:
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    return cmd, r.returncode, r.stdout + r.stderr
+
+
+def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -> Path:
+    if not force and up_to_date():
+        return LIB
+    nvcc = _nvcc()
+    BUILD.mkdir(parents=True, exist_ok=True)
+    objs = []
+    cmds = []
+    for src in _sources():
+        obj = BUILD / (src.stem + ".o")
+        objs.append(obj)
+        cmds.append([nvcc, *ARCH, *FLAGS, "-Xptxas", "-v", "-dc", str(src), "-o", str(obj)])
+    jobs = jobs or min(len(cmds), os.cpu_count() or 4)
+    with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
+        for cmd, rc, out in ex.map(_run, cmds):
+            if verbose:
+                print(out)
+            if rc != 0:
+                raise RuntimeError(f"nvcc failed ({rc}): {' '.join(cmd)}\n{out}")
+            (BUILD / (Path(cmd[-3]).stem + ".ptxas.txt")).write_text(out)
+    tmp = LIB.with_suffix(".so.tmp")
+    link = [nvcc, *ARCH, "-rdc=true", "-shared", "-cudart", "shared", *map(str, objs), "-o", str(tmp)]
+    cmd, rc, out = _run(link)
+    if rc != 0:
+        raise RuntimeError(f"link failed ({rc}): {' '.join(cmd)}\n{out}")
+    os.replace(tmp, LIB)
+    STAMP.write_text(_digest() + "\n")
+    return LIB
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("--jobs", type=int, default=None)
+    ap.add_argument("-v", "--verbose", action="store_true")
+    a = ap.parse_args()
+    print(build(force=a.force, jobs=a.jobs, verbose=a.verbose))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,329 @@
+// sy_abi.cu -- the extern "C" entry points declared in include/switchyard_b200.h:
+// argument validation, kernel planning and dispatch. No device allocation
+// happens anywhere in this library.
+#include <climits>
+#include <cstdio>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "sy_tile.cuh"
+
+namespace sy {
+
+__device__ unsigned int g_device_error = 0;
+
+namespace {
+
+constexpr int64_t kMaxD = 1 << 24;  // D is converted to float exactly below 2^24
+constexpr int kMaxDevices = 64;
+
+struct DevInfo {
+  int sms = 0;
+  int max_smem = 0;  // opt-in dynamic shared memory per block
+};
+
+cudaError_t dev_info(DevInfo* out) {
+  static std::mutex mu;
+  static DevInfo cache[kMaxDevices];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache[dev].sms == 0) {
+    DevInfo d;
+    e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    e = cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    cache[dev] = d;
+  }
+  *out = cache[dev];
+  return cudaSuccess;
+}
+
+int esize_of(int dtype) {
+  switch (dtype) {
+    case SY_BF16:
+    case SY_F16:
+      return 2;
+    case SY_F32:
+      return 4;
+    default:
+      return 0;
+  }
+}
+
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int64_t stats_stride(int64_t N) { return ((2 * N + 2) + 3) / 4 * 4; }
+
+enum TileOp { kOpFwd = 0, kOpBwd = 1, kOpSol = 2 };
+
+struct TilePlan {
+  bool ok = false;
+  TileCfg c{};
+  int grid = 0;
+  int cpt = 0;
+};
+
+// Choose the tile-kernel configuration for a shape, or report that the shape
+// needs the generic kernels (ok == false). Pointer alignment is checked by
+// the caller.
+TilePlan plan_tile(int op, int64_t N, int64_t BT, int64_t D, int dtype, const DevInfo& di) {
+  TilePlan p;
+  const int es = esize_of(dtype);
+  if (!es || N < 1 || N > kTileMaxN || D < 1 || D > kMaxD || BT < 1 || BT > INT_MAX) return p;
+  if ((D * es) % 16) return p;
+  const int64_t rc = D * es / 16;  // 16-byte chunks per row
+  // Chunks per thread: prefer 2 (two independent 16-byte loads per row per
+  // thread), then 1, then 4; group width is a multiple of a warp.
+  int cpt = 0, tg = 0;
+  const int cands[3] = {2, 1, 4};
+  for (int cand : cands) {
+    const int64_t t = ((rc + cand - 1) / cand + 31) / 32 * 32;
+    if (t <= kConsumerThreads && (rc + t - 1) / t <= cand) {
+      cpt = cand;
+      tg = (int)t;
+      break;
+    }
+  }
+  if (!cpt) return p;
+  int groups = kConsumerThreads / tg;
+  if (groups < 1) groups = 1;
+
+  TileCfg c{};
+  c.BT = BT;
+  c.N = (int)N;
+  c.D = (int)D;
+  c.row_chunks = (int)rc;
+  c.row_bytes = (int)(D * es);
+  c.stats_stride = (int)stats_stride(N);
+  c.red_stride = tile_red_stride((int)N);
+  c.coef_stride = tile_coef_stride((int)N);
+  c.tg = tg;
+  c.groups = groups;
+  int64_t body = N * c.row_bytes;
+  if (op == kOpBwd) body = (N + 1) * c.row_bytes + (int64_t)c.stats_stride * 4;
+  const int64_t stage = (body + 127) / 128 * 128;
+  if (stage > INT_MAX / 4) return p;
+  c.stage_bytes = (int)stage;
+  c.stages = 0;
+  const int64_t fixed = (int64_t)tile_smem_layout(c).total;
+  int64_t stages = (di.max_smem - fixed) / (stage + 2 * (int64_t)sizeof(uint64_t));
+  if (stages > 32) stages = 32;
+  if (stages < 2) return p;
+  if (groups > stages - 1) groups = (int)(stages - 1);
+  c.groups = groups;
+  c.stages = (int)stages;
+  if ((int64_t)tile_smem_layout(c).total > di.max_smem) return p;
+  p.ok = true;
+  p.c = c;
+  p.cpt = cpt;
+  p.grid = (int)(BT < di.sms ? BT : di.sms);
+  return p;
+}
+
+int generic_grid(int64_t BT, const DevInfo& di) {
+  const int64_t g = (int64_t)di.sms * 4;
+  return (int)(BT < g ? BT : g);
+}
+
+int64_t generic_partials(int64_t BT, const DevInfo& di) {
+  const int64_t g = (int64_t)di.sms * 2;
+  const int64_t p = BT < g ? BT : g;
+  return p < 1 ? 1 : p;
+}
+
+thread_local char t_last_error[256] = "";
+
+int cuda_status(cudaError_t e, const char* where) {
+  if (e == cudaSuccess) return SY_OK;
+  snprintf(t_last_error, sizeof(t_last_error), "%s: %s", where, cudaGetErrorString(e));
+  return SY_ERR_CUDA;
+}
+
+bool generic_fwd_fits(int64_t N, const DevInfo& di) {
+  return N <= kGenericMaxN && (N * 8 * 2 + 3 * N) * 4 <= di.max_smem;
+}
+
+bool generic_batched_fits(int64_t N, int64_t S, const DevInfo& di) {
+  return (N * (S + 1) * 8 + S * N) * 4 <= di.max_smem;
+}
+
+}  // namespace
+}  // namespace sy
+
+using namespace sy;
+
+extern "C" {
+
+const char* sy_status_string(int status) {
+  switch (status) {
+    case SY_OK:
+      return "ok";
+    case SY_ERR_ARG:
+      return "invalid argument (shape, size or null pointer)";
+    case SY_ERR_DTYPE:
+      return "unknown dtype code";
+    case SY_ERR_UNSUPPORTED:
+      return "shape outside the kernels' limits";
+    case SY_ERR_CUDA:
+      return t_last_error[0] ? t_last_error : "CUDA error";
+    case SY_ERR_DEVICE:
+      return "a kernel recorded a device-side error (bounded wait expired)";
+    default:
+      return "unknown status";
+  }
+}
+
+const char* sy_version(void) { return "switchyard-b200 0.1.0 (sm_100a)"; }
+
+int64_t sy_stats_stride(int64_t N) { return N < 1 ? 0 : stats_stride(N); }
+
+int sy_fwd(const void* v, const void* w, void* out, float* stats, int64_t N, int64_t BT,
+           int64_t D, int dtype, int w_dtype, float eps, sy_stream_t stream) {
+  if (!esize_of(dtype) || !esize_of(w_dtype)) return SY_ERR_DTYPE;
+  if (N < 1 || BT < 0 || D < 0) return SY_ERR_ARG;
+  if (BT == 0 || D == 0) return SY_OK;
+  if (!v || !w || !out) return SY_ERR_ARG;
+  if (D > kMaxD || BT > INT_MAX) return SY_ERR_UNSUPPORTED;
+  DevInfo di;
+  cudaError_t e = dev_info(&di);
+  if (e != cudaSuccess) return cuda_status(e, "sy_fwd: device query");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const TilePlan p = plan_tile(kOpFwd, N, BT, D, dtype, di);
+  if (p.ok && al16(v) && al16(out)) {
+    e = launch_tile_fwd(p.c, p.grid, p.cpt, dtype, v, w, w_dtype, out, stats, st);
+    return cuda_status(e, "sy_fwd: tile kernel launch");
+  }
+  if (!generic_fwd_fits(N, di)) return SY_ERR_UNSUPPORTED;
+  e = launch_generic_fwd(BT, (int)N, (int)D, dtype, v, w, w_dtype, out, stats,
+                         (int)stats_stride(N), eps, generic_grid(BT, di), st);
+  return cuda_status(e, "sy_fwd: generic kernel launch");
+}
+
+int64_t sy_bwd_partials(int64_t N, int64_t BT, int64_t D, int dtype) {
+  if (!esize_of(dtype) || N < 1 || BT < 0 || D < 0) return -SY_ERR_ARG;
+  if (BT == 0 || D == 0) return 1;
+  DevInfo di;
+  if (dev_info(&di) != cudaSuccess) return -SY_ERR_CUDA;
+  const TilePlan p = plan_tile(kOpBwd, N, BT, D, dtype, di);
+  if (p.ok) return (int64_t)p.grid * p.c.groups;
+  return generic_partials(BT, di);
+}
+
+int sy_bwd(const void* v, const void* w, const void* g, const float* stats, void* dv,
+           float* dw_partial, int64_t P, int64_t N, int64_t BT, int64_t D, int dtype,
+           int w_dtype, float eps, sy_stream_t stream) {
+  if (!esize_of(dtype) || !esize_of(w_dtype)) return SY_ERR_DTYPE;
+  if (N < 1 || BT < 0 || D < 0 || P < 1) return SY_ERR_ARG;
+  if (P != sy_bwd_partials(N, BT, D, dtype)) return SY_ERR_ARG;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D == 0) return SY_OK;
+  if (!dw_partial) return SY_ERR_ARG;
+  if (BT == 0) {
+    return cuda_status(cudaMemsetAsync(dw_partial, 0, (size_t)P * D * sizeof(float), st),
+                       "sy_bwd: zero dw_partial");
+  }
+  if (!v || !w || !g || !stats || !dv) return SY_ERR_ARG;
+  if (D > kMaxD || BT > INT_MAX) return SY_ERR_UNSUPPORTED;
+  DevInfo di;
+  cudaError_t e = dev_info(&di);
+  if (e != cudaSuccess) return cuda_status(e, "sy_bwd: device query");
+  const TilePlan p = plan_tile(kOpBwd, N, BT, D, dtype, di);
+  if (p.ok && al16(v) && al16(g) && al16(stats) && al16(dv) && al16(dw_partial)) {
+    e = launch_tile_bwd(p.c, p.grid, p.cpt, dtype, v, w, w_dtype, g, stats, dv, dw_partial, st);
+    return cuda_status(e, "sy_bwd: tile kernel launch");
+  }
+  if (N > kGenericMaxN || (N * 8 + 3 * N) * 4 > di.max_smem) return SY_ERR_UNSUPPORTED;
+  e = launch_generic_bwd(BT, (int)N, (int)D, dtype, v, w, w_dtype, g, stats, (int)stats_stride(N),
+                         dv, dw_partial, (int)P, eps, st);
+  return cuda_status(e, "sy_bwd: generic kernel launch");
+}
+
+int sy_dw_reduce(const float* dw_partial, int64_t P, int64_t D, void* dw, int dw_dtype,
+                 sy_stream_t stream) {
+  if (!esize_of(dw_dtype)) return SY_ERR_DTYPE;
+  if (P < 1 || D < 0) return SY_ERR_ARG;
+  if (D == 0) return SY_OK;
+  if (!dw_partial || !dw) return SY_ERR_ARG;
+  if (D > kMaxD) return SY_ERR_UNSUPPORTED;
+  const cudaError_t e =
+      launch_dw_reduce(dw_partial, P, D, dw, dw_dtype, true, static_cast<cudaStream_t>(stream));
+  return cuda_status(e, "sy_dw_reduce: launch");
+}
+
+int sy_fwd_batched(const void* v, const void* queries, void* out, int64_t N, int64_t BT, int64_t D,
+                   int64_t S, int dtype, float eps, sy_stream_t stream) {
+  if (!esize_of(dtype)) return SY_ERR_DTYPE;
+  if (N < 1 || BT < 0 || D < 0 || S < 1) return SY_ERR_ARG;
+  if (BT == 0 || D == 0) return SY_OK;
+  if (!v || !queries || !out) return SY_ERR_ARG;
+  if (D > kMaxD || BT > INT_MAX || S > INT_MAX) return SY_ERR_UNSUPPORTED;
+  if (S == 1) return sy_fwd(v, queries, out, nullptr, N, BT, D, dtype, dtype, eps, stream);
+  DevInfo di;
+  cudaError_t e = dev_info(&di);
+  if (e != cudaSuccess) return cuda_status(e, "sy_fwd_batched: device query");
+  if (!generic_batched_fits(N, S, di)) return SY_ERR_UNSUPPORTED;
+  e = launch_generic_batched(BT, (int)N, (int)D, (int)S, dtype, v, queries, out, eps,
+                             generic_grid(BT, di), static_cast<cudaStream_t>(stream));
+  return cuda_status(e, "sy_fwd_batched: generic kernel launch");
+}
+
+int sy_speed_of_light(const void* v, void* out, int64_t N, int64_t BT, int64_t D, int dtype,
+                      sy_stream_t stream) {
+  if (!esize_of(dtype)) return SY_ERR_DTYPE;
+  if (N < 1 || BT < 0 || D < 0) return SY_ERR_ARG;
+  if (BT == 0 || D == 0) return SY_OK;
+  if (!v || !out) return SY_ERR_ARG;
+  if (D > kMaxD || BT > INT_MAX) return SY_ERR_UNSUPPORTED;
+  DevInfo di;
+  cudaError_t e = dev_info(&di);
+  if (e != cudaSuccess) return cuda_status(e, "sy_speed_of_light: device query");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const TilePlan p = plan_tile(kOpSol, N, BT, D, dtype, di);
+  if (p.ok && al16(v) && al16(out)) {
+    e = launch_tile_sol(p.c, p.grid, p.cpt, dtype, v, out, st);
+    return cuda_status(e, "sy_speed_of_light: tile kernel launch");
+  }
+  e = launch_generic_sol(BT, (int)N, (int)D, dtype, v, out, generic_grid(BT, di), st);
+  return cuda_status(e, "sy_speed_of_light: generic kernel launch");
+}
+
+int sy_plan_kind(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype) {
+  if (!esize_of(dtype)) return -SY_ERR_DTYPE;
+  if (N < 1 || BT < 0 || D < 0) return -SY_ERR_ARG;
+  DevInfo di;
+  if (dev_info(&di) != cudaSuccess) return -SY_ERR_CUDA;
+  const int64_t bt = BT < 1 ? 1 : BT;
+  switch (op) {
+    case 0:
+      return plan_tile(kOpFwd, N, bt, D, dtype, di).ok ? 1 : 0;
+    case 1:
+      return plan_tile(kOpBwd, N, bt, D, dtype, di).ok ? 1 : 0;
+    case 2:
+      if (S < 1) return -SY_ERR_ARG;
+      if (S == 1) return plan_tile(kOpFwd, N, bt, D, dtype, di).ok ? 1 : 0;
+      return 0;
+    default:
+      return -SY_ERR_ARG;
+  }
+}
+
+int sy_device_error(int* code) {
+  if (!code) return SY_ERR_ARG;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_status(e, "sy_device_error: synchronize");
+  unsigned int v = 0;
+  e = cudaMemcpyFromSymbol(&v, g_device_error, sizeof(v));
+  if (e != cudaSuccess) return cuda_status(e, "sy_device_error: read");
+  const unsigned int zero = 0;
+  e = cudaMemcpyToSymbol(g_device_error, &zero, sizeof(zero));
+  if (e != cudaSuccess) return cuda_status(e, "sy_device_error: clear");
+  *code = (int)v;
+  return SY_OK;
+}
+
+}  // extern "C"

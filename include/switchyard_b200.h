@@ -1,0 +1,151 @@
+/*
+ * switchyard_b200.h -- C ABI of the B200 (sm_100a) Block AttnRes operator.
+ *
+ * The operator, per token (b, t), over N source rows v[n, b, t, :] of length D
+ * and one query w[D]:
+ *
+ *     r_n     = 1 / sqrt(mean_d v[n,d]^2 + eps)        inverse RMS of source n
+ *     logit_n = r_n * sum_d w[d] v[n,d]                 no 1/sqrt(D) scale
+ *     alpha   = softmax_n(logit)                        over the source axis
+ *     out[d]  = sum_n alpha_n v[n,d]                    raw (unnormalised) v
+ *
+ * Everything here is plain C: raw device pointers, element counts, a dtype
+ * code and a CUDA stream passed as `void*` (a cudaStream_t; NULL means the
+ * legacy default stream). No entry point allocates device memory; callers own
+ * every buffer. Launches are asynchronous on the given stream. Every function
+ * returns SY_OK or a nonzero status (see sy_status_string); none of them
+ * traps or aborts on bad input.
+ *
+ * Layouts (all row-major, contiguous):
+ *   v      [N, BT, D]      BT = B*T tokens; element (n,tok,d) at (n*BT+tok)*D+d
+ *   out    [BT, D]         dtype of v
+ *   w      [D]             any of the three dtypes (w_dtype)
+ *   stats  [BT, SW] fp32   SW = sy_stats_stride(N); per token:
+ *                          logit[0..N), r[0..N), max logit m, logsumexp lse
+ *   g      [BT, D]         upstream gradient, dtype of v
+ *   dv     [N, BT, D]      dtype of v
+ *   dw_partial [P, D] fp32 P = sy_bwd_partials(...) rows, reduced by
+ *                          sy_dw_reduce in a fixed order (deterministic)
+ *   queries [S, D], out_batched [S, BT, D]   dtype of v
+ *
+ * The reference this replaces is Python/Triton (sabdulmajid/blackwell-switchyard,
+ * src/switchyard/triton_op.py); it has no C interface of its own. Each entry
+ * point below names the reference function whose job it takes over.
+ */
+#ifndef SWITCHYARD_B200_H
+#define SWITCHYARD_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+#define SY_BF16 0
+#define SY_F16 1
+#define SY_F32 2
+
+/* status codes */
+#define SY_OK 0
+#define SY_ERR_ARG 1         /* bad shape, size or null pointer              */
+#define SY_ERR_DTYPE 2       /* unknown dtype code                           */
+#define SY_ERR_UNSUPPORTED 3 /* shape outside every kernel's limits          */
+#define SY_ERR_CUDA 4        /* a CUDA runtime call or launch failed         */
+#define SY_ERR_DEVICE 5      /* a kernel reported a device-side error word   */
+
+typedef void* sy_stream_t; /* a cudaStream_t */
+
+/* Exported symbols; everything else in the library is hidden. */
+#if defined(__GNUC__)
+#define SY_API __attribute__((visibility("default")))
+#else
+#define SY_API
+#endif
+
+/* Human-readable text for a status code (static storage). */
+SY_API const char* sy_status_string(int status);
+
+/* Library version string (static storage). */
+SY_API const char* sy_version(void);
+
+/* Floats per token in the statistics buffer written by sy_fwd:
+ * round_up(2*N + 2, 4). */
+SY_API int64_t sy_stats_stride(int64_t N);
+
+/*
+ * Forward. Replaces _BlockAttnResTriton.forward and its kernels
+ * _fwd_resident/_fwd_tiled (src/switchyard/triton_op.py:504-536, :50-117).
+ * `stats` may be NULL (inference); when given it must hold BT*sy_stats_stride(N)
+ * floats and is what sy_bwd reads.
+ */
+SY_API int sy_fwd(const void* v, const void* w, void* out, float* stats, int64_t N,
+           int64_t BT, int64_t D, int dtype, int w_dtype, float eps,
+           sy_stream_t stream);
+
+/*
+ * Number of dw partial rows sy_bwd writes for this shape on the current
+ * device (>= 1). Replaces nothing in the reference: its backward used one
+ * fp32 accumulator with atomics (src/switchyard/triton_op.py:547-550, :264).
+ */
+SY_API int64_t sy_bwd_partials(int64_t N, int64_t BT, int64_t D, int dtype);
+
+/*
+ * Backward from saved statistics. Replaces _BlockAttnResTriton.backward with
+ * _bwd_resident / _bwd_stats / _bwd_apply (src/switchyard/triton_op.py:538-589,
+ * :194-375). Writes every element of dv and every row of dw_partial
+ * (P = sy_bwd_partials rows of D fp32); no zero-fill is needed beforehand.
+ */
+SY_API int sy_bwd(const void* v, const void* w, const void* g, const float* stats,
+           void* dv, float* dw_partial, int64_t P, int64_t N, int64_t BT,
+           int64_t D, int dtype, int w_dtype, float eps, sy_stream_t stream);
+
+/*
+ * dw[d] = sum_{p=0..P-1} dw_partial[p, d], summed in a fixed order and
+ * written in dw_dtype. Replaces the reference's torch.zeros fill and the
+ * dw.to(w.dtype) cast (src/switchyard/triton_op.py:550, :563, :589).
+ */
+SY_API int sy_dw_reduce(const float* dw_partial, int64_t P, int64_t D, void* dw,
+                 int dw_dtype, sy_stream_t stream);
+
+/*
+ * Batched-query forward, output only: out[s] = forward(v, queries[s]).
+ * Replaces block_attn_res_batched and _fwd_batched_resident
+ * (src/switchyard/triton_op.py:438-501, :378-414), including the shapes the
+ * reference sent to its per-query fallback loop.
+ */
+SY_API int sy_fwd_batched(const void* v, const void* queries, void* out, int64_t N,
+                   int64_t BT, int64_t D, int64_t S, int dtype, float eps,
+                   sy_stream_t stream);
+
+/*
+ * Speed-of-light ceiling: out[tok, d] = sum_n v[n, tok, d]. Same bytes and
+ * access pattern as sy_fwd without the softmax. Replaces speed_of_light /
+ * _speed_of_light (src/switchyard/triton_op.py:153-191).
+ */
+SY_API int sy_speed_of_light(const void* v, void* out, int64_t N, int64_t BT,
+                      int64_t D, int dtype, sy_stream_t stream);
+
+/*
+ * Which kernel family sy_fwd / sy_bwd / sy_fwd_batched would launch for a
+ * shape, without launching: 1 = TMA-pipelined tile kernel, 2 = cluster
+ * D-split tile kernel, 0 = generic (any stride/size) kernel, <0 = error.
+ * `op` is 0 forward, 1 backward, 2 batched (S queries). Used by tests to pin
+ * dispatch, like the reference's _launch_config tests.
+ */
+SY_API int sy_plan_kind(int op, int64_t N, int64_t BT, int64_t D, int64_t S,
+                 int dtype);
+
+/*
+ * Reads the device-side error word of the current device (set when a
+ * kernel's bounded wait ran out) and clears it. Synchronises the device.
+ * Writes 0 to *code when no error was recorded.
+ */
+SY_API int sy_device_error(int* code);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SWITCHYARD_B200_H */

@@ -1,0 +1,84 @@
+"""The C-ABI library on the CPU: it loads, exports every entry point the header
+declares, and validates arguments on the host before any CUDA call. No test
+here launches a kernel."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def _declared() -> set[str]:
+    names = set()
+    for h in HEADERS:
+        text = h.read_text()
+        names |= set(re.findall(r"^SY_API\s+[\w\s\*]+?\b(sy_\w+)\s*\(", text, flags=re.M))
+    return names
+
+
+@pytest.fixture(scope="module")
+def native():
+    from switchyard import _native
+
+    return _native
+
+
+def test_header_declares_the_entry_points():
+    names = _declared()
+    for required in ("sy_fwd", "sy_bwd", "sy_bwd_partials", "sy_dw_reduce", "sy_fwd_batched",
+                     "sy_speed_of_light", "sy_stats_stride", "sy_status_string"):
+        assert required in names
+
+
+def test_library_exports_every_declared_symbol(native):
+    lib = ctypes.CDLL(str(native.LIB_PATH))
+    for name in sorted(_declared()):
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+        assert name in native.SIGNATURES, f"{name} has no ctypes signature in _native"
+
+
+def test_library_is_built_for_sm100a_only():
+    """The build compiles for sm_100a and nothing else (no PTX for JIT)."""
+    import build
+
+    assert build.ARCH == ["-gencode", "arch=compute_100a,code=sm_100a"]
+
+
+def test_status_strings(native):
+    for code in range(6):
+        assert native.lib.sy_status_string(code)
+    assert native.lib.sy_version().startswith(b"switchyard-b200")
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 9, 16, 33, 64])
+def test_stats_stride(native, n):
+    assert native.stats_stride(n) == (2 * n + 2 + 3) // 4 * 4
+    assert native.stats_stride(n) % 4 == 0  # 16-byte rows for the bulk copy
+
+
+def test_host_validation_rejects_bad_arguments(native):
+    L = native.lib
+    bf16, bad = native.SY_BF16, 7
+    # unknown dtype codes
+    assert L.sy_fwd(1, 1, 1, None, 2, 4, 8, bad, bf16, 1e-6, None) == native.SY_ERR_DTYPE
+    assert L.sy_fwd(1, 1, 1, None, 2, 4, 8, bf16, bad, 1e-6, None) == native.SY_ERR_DTYPE
+    assert L.sy_fwd_batched(1, 1, 1, 2, 4, 8, 2, bad, 1e-6, None) == native.SY_ERR_DTYPE
+    # bad sizes and null pointers
+    assert L.sy_fwd(1, 1, 1, None, 0, 4, 8, bf16, bf16, 1e-6, None) == native.SY_ERR_ARG
+    assert L.sy_fwd(None, 1, 1, None, 2, 4, 8, bf16, bf16, 1e-6, None) == native.SY_ERR_ARG
+    assert L.sy_fwd(1, 1, 1, None, 2, -1, 8, bf16, bf16, 1e-6, None) == native.SY_ERR_ARG
+    assert L.sy_fwd_batched(1, 1, 1, 2, 4, 8, 0, bf16, 1e-6, None) == native.SY_ERR_ARG
+    assert L.sy_dw_reduce(None, 0, 8, None, bf16, None) == native.SY_ERR_ARG
+    assert L.sy_speed_of_light(None, 1, 2, 4, 8, bf16, None) == native.SY_ERR_ARG
+    # empty problems are a successful no-op (no launch, no CUDA call)
+    assert L.sy_fwd(None, None, None, None, 2, 0, 8, bf16, bf16, 1e-6, None) == native.SY_OK
+    assert L.sy_fwd(None, None, None, None, 2, 4, 0, bf16, bf16, 1e-6, None) == native.SY_OK
+    assert L.sy_dw_reduce(None, 1, 0, None, bf16, None) == native.SY_OK
+    assert L.sy_bwd_partials(3, 0, 16, bf16) == 1
+    assert L.sy_bwd_partials(0, 4, 16, bf16) < 0
