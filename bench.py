@@ -2,10 +2,13 @@
 
 Workload (one "step"): forward + backward of ``block_attn_res_triton`` at
 N=9, B=1, T=4096, D=2048 bf16 with v ~ N(0,1), w ~ N(0,1/D), dout ~ N(0,1)
-(synthetic; the reference uses no dataset). L2 (126 MB) is flushed with a
-384 MiB memset before every timed step, outside that step's CUDA events, and a
-short spin kernel lets the host queue the whole step before it starts, so the
-events see device time only.
+(synthetic; the reference uses no dataset). Before every timed step, outside
+that step's CUDA events, L2 (126 MB) is flushed: a 384 MiB buffer is written
+(as the reference harness does, bench/harness.py:73-77) and then a separate
+256 MiB buffer is read, so the L2 holds only clean, unrelated lines and the
+flush's own dirty write-back is not charged to the step. A short spin kernel
+then lets the host queue the whole step before it starts, so the events see
+device time only.
 
 Printed: ONE JSON line (rank 0). ``value`` = achieved HBM TB/s of the step's
 algorithmic bytes, (3N+2)*B*T*D*2 per rank, summed over ranks, divided by the
@@ -26,6 +29,7 @@ fwd+bwd on a bounded token sample on all host threads; rank 0 only.
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import json
 import math
 import os
@@ -61,6 +65,10 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline budget")
     ap.add_argument("--no-extras", action="store_true", help="skip batched/SoL/e2e extras")
+    ap.add_argument("--profile", choices=["fwd", "bwd", "step", "sol", "batched8", "batched16"],
+                    default=None,
+                    help="no timing: run 5 launches of one kernel (or step) at the representative "
+                         "shape, for an ncu capture; prints nothing")
     return ap.parse_args()
 
 
@@ -111,7 +119,11 @@ class ClockSampler:
             import pynvml
 
             pynvml.nvmlInit()
-            bus = torch.cuda.get_device_properties(device_index).pci_bus_id
+            props = torch.cuda.get_device_properties(device_index)
+            # NVML wants the "DDDDDDDD:BB:DD.F" string; torch reports integers.
+            bus = "{:08X}:{:02X}:{:02X}.0".format(
+                int(getattr(props, "pci_domain_id", 0)), int(props.pci_bus_id),
+                int(props.pci_device_id)).encode()
             try:
                 self.h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
             except Exception:  # noqa: BLE001
@@ -126,9 +138,10 @@ class ClockSampler:
         nv = self.nv
         while not self._stop.is_set():
             try:
-                mhz = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
-                mask = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
-                self.samples.append(mhz)
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or getattr(
+                    nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+                mask = get(self.h)
                 for name, bit in self.REASONS.items():
                     if mask & bit:
                         self.reasons.add(name)
@@ -161,6 +174,21 @@ class ClockSampler:
 # ----------------------------------------------------------------------------- timing
 
 
+class L2Flush:
+    """Write 384 MiB (evicting every line of the 126 MB L2), then read 256 MiB
+    of another buffer so the written lines are flushed back to HBM before the
+    timed region and L2 holds only clean lines unrelated to the step."""
+
+    def __init__(self, dev):
+        self.w = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+        self.r = torch.zeros(64 * 2**20, dtype=torch.float32, device=dev)
+        self.o = torch.empty((), dtype=torch.float32, device=dev)
+
+    def __call__(self):
+        self.w.zero_()
+        torch.sum(self.r, dim=0, out=self.o)
+
+
 def timed_steps(fn, steps, flush, lead_cycles=400_000):
     """Per-step device times (ms): flush L2, let a spin kernel cover the host's
     queueing of the step, then bracket only the step with CUDA events on the
@@ -168,7 +196,7 @@ def timed_steps(fn, steps, flush, lead_cycles=400_000):
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for i in range(steps):
-        flush.zero_()
+        flush()
         torch.cuda._sleep(lead_cycles)
         starts[i].record()
         fn()
@@ -330,7 +358,7 @@ def run_ours(args):
 
     n, b, t, d = REP
     v, w, dout = make_inputs(dev, rank, n, b, t, d)
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
     op = block_attn_res_triton if world == 1 else block_attn_res_sharded
 
     def step():
@@ -391,7 +419,8 @@ def run_ours(args):
             "config": {
                 "workload": "Block AttnRes forward+backward (block_attn_res_triton, autograd) per step",
                 "N": n, "B": b, "T": t, "D": d, "tokens_per_rank": b * t,
-                "l2": "flushed (384 MiB memset) before every timed step, outside its events",
+                "l2": "flushed before every timed step, outside its events: 384 MiB written, "
+                      "then 256 MiB of another buffer read (no dirty flush lines left in L2)",
                 "parallelism": f"token-axis shards x{world}" if world > 1 else "single GPU",
             },
             "fwd_us": mean_fwd * 1e3,
@@ -514,8 +543,46 @@ def run_reference(args):
     }), flush=True)
 
 
+def run_profile(kind: str):
+    """A handful of launches at the representative shape and nothing else, so
+    that an ncu capture ends by itself in seconds."""
+    from switchyard import _native, block_attn_res_batched, block_attn_res_triton
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    n, b, t, d = REP
+    v, w, dout = make_inputs(dev, 0, n, b, t, d)
+    bt = b * t
+    out = torch.empty(b, t, d, device=dev, dtype=v.dtype)
+    stats = torch.empty(bt, _native.stats_stride(n), device=dev, dtype=torch.float32)
+    dv = torch.empty_like(v)
+    part = torch.empty(_native.bwd_partials(n, bt, d, v.dtype), d, device=dev, dtype=torch.float32)
+    if kind == "bwd":
+        _native.fwd(v, w, out, stats, n, bt, d, 1e-6)
+    q = (torch.randn(16, d, device=dev) / math.sqrt(d)).to(v.dtype)
+    for _ in range(5):
+        if kind == "fwd":
+            _native.fwd(v, w, out, stats, n, bt, d, 1e-6)
+        elif kind == "bwd":
+            _native.bwd(v, w, dout, stats, dv, part, n, bt, d, 1e-6)
+        elif kind == "sol":
+            _native.speed_of_light(v, out, n, bt, d)
+        elif kind == "step":
+            vv = v.detach().requires_grad_(True)
+            ww = w.detach().requires_grad_(True)
+            block_attn_res_triton(vv, ww).backward(dout)
+        elif kind.startswith("batched"):
+            with torch.no_grad():
+                block_attn_res_batched(v, q[: int(kind[len("batched"):])])
+    torch.cuda.synchronize()
+
+
 def main():
+    faulthandler.enable()
     args = parse_args()
+    if args.profile:
+        run_profile(args.profile)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -78,17 +78,23 @@ def _run(cmd: list[str]) -> tuple[list[str], int, str]:
     return cmd, r.returncode, r.stdout + r.stderr
 
 
-def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -> Path:
-    if not force and up_to_date():
+def build(force: bool = False, jobs: int | None = None, verbose: bool = False,
+          defines: tuple[str, ...] = (), out: Path | None = None) -> Path:
+    """Build the library. ``defines`` (``NAME=VALUE``) and ``out`` build a
+    variant elsewhere (tuning experiments) without touching the in-tree one."""
+    lib = Path(out) if out is not None else LIB
+    if not force and not defines and out is None and up_to_date():
         return LIB
     nvcc = _nvcc()
-    BUILD.mkdir(parents=True, exist_ok=True)
+    bdir = BUILD if out is None else lib.parent / (lib.stem + "_obj")
+    bdir.mkdir(parents=True, exist_ok=True)
+    dflags = [f"-D{d}" for d in defines]
     objs = []
     cmds = []
     for src in _sources():
-        obj = BUILD / (src.stem + ".o")
+        obj = bdir / (src.stem + ".o")
         objs.append(obj)
-        cmds.append([nvcc, *ARCH, *FLAGS, "-Xptxas", "-v", "-dc", str(src), "-o", str(obj)])
+        cmds.append([nvcc, *ARCH, *FLAGS, *dflags, "-Xptxas", "-v", "-dc", str(src), "-o", str(obj)])
     jobs = jobs or min(len(cmds), os.cpu_count() or 4)
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
         for cmd, rc, out in ex.map(_run, cmds):
@@ -96,15 +102,16 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
                 print(out)
             if rc != 0:
                 raise RuntimeError(f"nvcc failed ({rc}): {' '.join(cmd)}\n{out}")
-            (BUILD / (Path(cmd[-3]).stem + ".ptxas.txt")).write_text(out)
-    tmp = LIB.with_suffix(".so.tmp")
+            (bdir / (Path(cmd[-3]).stem + ".ptxas.txt")).write_text(out)
+    tmp = lib.with_suffix(".so.tmp")
     link = [nvcc, *ARCH, "-rdc=true", "-shared", "-cudart", "shared", *map(str, objs), "-o", str(tmp)]
     cmd, rc, out = _run(link)
     if rc != 0:
         raise RuntimeError(f"link failed ({rc}): {' '.join(cmd)}\n{out}")
-    os.replace(tmp, LIB)
-    STAMP.write_text(_digest() + "\n")
-    return LIB
+    os.replace(tmp, lib)
+    if out is None and not defines:
+        STAMP.write_text(_digest() + "\n")
+    return lib
 
 
 def main() -> int:

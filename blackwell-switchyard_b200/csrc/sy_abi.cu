@@ -7,7 +7,20 @@
 #include <cstring>
 #include <mutex>
 
+#include "sy_reg.cuh"
 #include "sy_tile.cuh"
+
+// Planner tuning knobs. The defaults are the shipped configuration; builds
+// with other values exist only for tuning sweeps.
+#ifndef SY_TUNE_MAX_STAGES
+#define SY_TUNE_MAX_STAGES 32
+#endif
+#ifndef SY_TUNE_GROUPS
+#define SY_TUNE_GROUPS 0  // 0: as many groups as fit 256 consumer threads
+#endif
+#ifndef SY_TUNE_CTAS_PER_SM
+#define SY_TUNE_CTAS_PER_SM 1
+#endif
 
 namespace sy {
 
@@ -60,38 +73,63 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 int64_t stats_stride(int64_t N) { return ((2 * N + 2) + 3) / 4 * 4; }
 
 enum TileOp { kOpFwd = 0, kOpBwd = 1, kOpSol = 2 };
+enum PlanKind { kPlanGeneric = 0, kPlanRegTile = 1, kPlanSmemTile = 2 };
 
 struct TilePlan {
-  bool ok = false;
+  int kind = kPlanGeneric;
   TileCfg c{};
   int grid = 0;
   int cpt = 0;
+  int64_t smem = 0;
 };
 
-// Choose the tile-kernel configuration for a shape, or report that the shape
-// needs the generic kernels (ok == false). Pointer alignment is checked by
-// the caller.
+int64_t round32(int64_t x) { return (x + 31) / 32 * 32; }
+
+// Fill in stages/groups for a tile configuration whose tg, row and scratch
+// sizes are set. Returns false if fewer than two stages fit.
+bool size_ring(TileCfg& c, int op, int groups, const DevInfo& di, int64_t* smem_out,
+               bool per_group_rings = false) {
+  int64_t body = (int64_t)c.N * c.row_bytes;
+  if (op == kOpBwd) body = (int64_t)(c.N + 1) * c.row_bytes + (int64_t)c.stats_stride * 4;
+  const int64_t stage = (body + 127) / 128 * 128;
+  if (stage > INT_MAX / 4) return false;
+  c.stage_bytes = (int)stage;
+  c.groups = groups;
+  c.stages = 0;
+  const int64_t fixed = (int64_t)tile_smem_layout(c).total;
+  // Shared memory per CTA: the whole opt-in limit at one CTA per SM; with k
+  // CTAs per SM, a k-th of the SM's 228 KiB minus the 1 KiB each CTA reserves.
+  const int64_t budget = SY_TUNE_CTAS_PER_SM == 1
+                             ? di.max_smem
+                             : (int64_t)(233472 / SY_TUNE_CTAS_PER_SM) - 1024;
+  int64_t stages = (budget - fixed) / (stage + 2 * (int64_t)sizeof(uint64_t));
+  if (stages > SY_TUNE_MAX_STAGES) stages = SY_TUNE_MAX_STAGES;
+  if (stages < 2) return false;
+  // Group g consumes tokens k = g (mod G) from stage k mod S, waiting on the
+  // stage's barrier with parity (k / S) & 1. That parity test is only sound if
+  // the previous token of the same stage was consumed by the same group (then
+  // it has certainly landed): S must be a multiple of G. Each group also gets
+  // at least two stages, so one can load while it computes on the other.
+  // (The register-tile kernels give every group its own ring instead, which
+  // has no such constraint.)
+  while (groups > 1 && stages < 2 * groups) --groups;
+  if (!per_group_rings) stages = stages / groups * groups;
+  c.groups = groups;
+  c.stages = (int)stages;
+  const int64_t total = (int64_t)tile_smem_layout(c).total;
+  if (total > budget) return false;
+  *smem_out = total;
+  return true;
+}
+
+// Choose the kernel family and configuration for a shape. Pointer alignment
+// is checked by the caller (misaligned pointers take the generic kernels).
 TilePlan plan_tile(int op, int64_t N, int64_t BT, int64_t D, int dtype, const DevInfo& di) {
   TilePlan p;
   const int es = esize_of(dtype);
   if (!es || N < 1 || N > kTileMaxN || D < 1 || D > kMaxD || BT < 1 || BT > INT_MAX) return p;
   if ((D * es) % 16) return p;
   const int64_t rc = D * es / 16;  // 16-byte chunks per row
-  // Chunks per thread: prefer 2 (two independent 16-byte loads per row per
-  // thread), then 1, then 4; group width is a multiple of a warp.
-  int cpt = 0, tg = 0;
-  const int cands[3] = {2, 1, 4};
-  for (int cand : cands) {
-    const int64_t t = ((rc + cand - 1) / cand + 31) / 32 * 32;
-    if (t <= kConsumerThreads && (rc + t - 1) / t <= cand) {
-      cpt = cand;
-      tg = (int)t;
-      break;
-    }
-  }
-  if (!cpt) return p;
-  int groups = kConsumerThreads / tg;
-  if (groups < 1) groups = 1;
 
   TileCfg c{};
   c.BT = BT;
@@ -101,28 +139,90 @@ TilePlan plan_tile(int op, int64_t N, int64_t BT, int64_t D, int dtype, const De
   c.row_bytes = (int)(D * es);
   c.stats_stride = (int)stats_stride(N);
   c.red_stride = tile_red_stride((int)N);
-  c.coef_stride = tile_coef_stride((int)N);
+  const int64_t slots = (int64_t)di.sms * SY_TUNE_CTAS_PER_SM;
+  const int grid = (int)(BT < slots ? BT : slots);
+
+  // 1) register tile: exact-N kernels, the packed tile (N * CPT * 4 words)
+  //    held in registers; two chunks per thread up to N = 9, else one.
+  if (op != kOpSol && N <= kRegMaxN) {
+    int cpt = 0, tg = 0;
+    if (N <= kRegMaxN2) {
+      const int64_t t = round32((rc + 1) / 2);
+      if (t <= kConsumerThreads && (rc + t - 1) / t <= 2) cpt = 2, tg = (int)t;
+    }
+    if (!cpt && round32(rc) <= kConsumerThreads) cpt = 1, tg = (int)round32(rc);
+    if (cpt) {
+      TileCfg rcfg = c;
+      rcfg.tg = tg;
+      rcfg.coef_stride = 0;
+      int groups = kConsumerThreads / tg;
+      if (SY_TUNE_GROUPS > 0) groups = SY_TUNE_GROUPS;
+      if (size_ring(rcfg, op, groups < 1 ? 1 : groups, di, &p.smem, /*per_group_rings=*/true)) {
+        p.kind = kPlanRegTile;
+        p.c = rcfg;
+        p.cpt = cpt;
+        p.grid = grid;
+        return p;
+      }
+    }
+  }
+
+  // 2) shared-memory tile: run-time N (up to kTileMaxN), rows re-read from
+  //    the stage in the weighted sum.
+  int cpt = 0, tg = 0;
+  const int cands[3] = {2, 1, 4};
+  for (int cand : cands) {
+    const int64_t t = round32((rc + cand - 1) / cand);
+    if (t <= kConsumerThreads && (rc + t - 1) / t <= cand) {
+      cpt = cand;
+      tg = (int)t;
+      break;
+    }
+  }
+  if (!cpt) return p;
   c.tg = tg;
-  c.groups = groups;
-  int64_t body = N * c.row_bytes;
-  if (op == kOpBwd) body = (N + 1) * c.row_bytes + (int64_t)c.stats_stride * 4;
-  const int64_t stage = (body + 127) / 128 * 128;
-  if (stage > INT_MAX / 4) return p;
-  c.stage_bytes = (int)stage;
-  c.stages = 0;
-  const int64_t fixed = (int64_t)tile_smem_layout(c).total;
-  int64_t stages = (di.max_smem - fixed) / (stage + 2 * (int64_t)sizeof(uint64_t));
-  if (stages > 32) stages = 32;
-  if (stages < 2) return p;
-  if (groups > stages - 1) groups = (int)(stages - 1);
-  c.groups = groups;
-  c.stages = (int)stages;
-  if ((int64_t)tile_smem_layout(c).total > di.max_smem) return p;
-  p.ok = true;
+  c.coef_stride = tile_coef_stride((int)N);
+  int groups = kConsumerThreads / tg;
+  if (SY_TUNE_GROUPS > 0) groups = SY_TUNE_GROUPS;
+  if (!size_ring(c, op, groups < 1 ? 1 : groups, di, &p.smem)) return p;
+  p.kind = kPlanSmemTile;
   p.c = c;
   p.cpt = cpt;
-  p.grid = (int)(BT < di.sms ? BT : di.sms);
+  p.grid = grid;
   return p;
+}
+
+cudaError_t launch_plan_fwd(const TilePlan& p, int dtype, const void* v, const void* w,
+                            int w_dtype, void* out, float* stats, cudaStream_t st) {
+  if (p.kind == kPlanRegTile) {
+    switch (dtype) {
+      case SY_BF16:
+        return launch_reg_fwd_bf16(p.c, p.grid, p.cpt, v, w, w_dtype, out, stats, st);
+      case SY_F16:
+        return launch_reg_fwd_f16(p.c, p.grid, p.cpt, v, w, w_dtype, out, stats, st);
+      case SY_F32:
+        return launch_reg_fwd_f32(p.c, p.grid, p.cpt, v, w, w_dtype, out, stats, st);
+    }
+    return cudaErrorInvalidValue;
+  }
+  return launch_tile_fwd(p.c, p.grid, p.cpt, dtype, v, w, w_dtype, out, stats, st);
+}
+
+cudaError_t launch_plan_bwd(const TilePlan& p, int dtype, const void* v, const void* w,
+                            int w_dtype, const void* g, const float* stats, void* dv, float* dwp,
+                            cudaStream_t st) {
+  if (p.kind == kPlanRegTile) {
+    switch (dtype) {
+      case SY_BF16:
+        return launch_reg_bwd_bf16(p.c, p.grid, p.cpt, v, w, w_dtype, g, stats, dv, dwp, st);
+      case SY_F16:
+        return launch_reg_bwd_f16(p.c, p.grid, p.cpt, v, w, w_dtype, g, stats, dv, dwp, st);
+      case SY_F32:
+        return launch_reg_bwd_f32(p.c, p.grid, p.cpt, v, w, w_dtype, g, stats, dv, dwp, st);
+    }
+    return cudaErrorInvalidValue;
+  }
+  return launch_tile_bwd(p.c, p.grid, p.cpt, dtype, v, w, w_dtype, g, stats, dv, dwp, st);
 }
 
 int generic_grid(int64_t BT, const DevInfo& di) {
@@ -194,8 +294,8 @@ int sy_fwd(const void* v, const void* w, void* out, float* stats, int64_t N, int
   if (e != cudaSuccess) return cuda_status(e, "sy_fwd: device query");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const TilePlan p = plan_tile(kOpFwd, N, BT, D, dtype, di);
-  if (p.ok && al16(v) && al16(out)) {
-    e = launch_tile_fwd(p.c, p.grid, p.cpt, dtype, v, w, w_dtype, out, stats, st);
+  if (p.kind != kPlanGeneric && al16(v) && al16(out)) {
+    e = launch_plan_fwd(p, dtype, v, w, w_dtype, out, stats, st);
     return cuda_status(e, "sy_fwd: tile kernel launch");
   }
   if (!generic_fwd_fits(N, di)) return SY_ERR_UNSUPPORTED;
@@ -210,7 +310,9 @@ int64_t sy_bwd_partials(int64_t N, int64_t BT, int64_t D, int dtype) {
   DevInfo di;
   if (dev_info(&di) != cudaSuccess) return -SY_ERR_CUDA;
   const TilePlan p = plan_tile(kOpBwd, N, BT, D, dtype, di);
-  if (p.ok) return (int64_t)p.grid * p.c.groups;
+  // register tile: one row per CTA; shared-memory tile: one row per group
+  if (p.kind == kPlanRegTile) return (int64_t)p.grid;
+  if (p.kind != kPlanGeneric) return (int64_t)p.grid * p.c.groups;
   return generic_partials(BT, di);
 }
 
@@ -233,8 +335,9 @@ int sy_bwd(const void* v, const void* w, const void* g, const float* stats, void
   cudaError_t e = dev_info(&di);
   if (e != cudaSuccess) return cuda_status(e, "sy_bwd: device query");
   const TilePlan p = plan_tile(kOpBwd, N, BT, D, dtype, di);
-  if (p.ok && al16(v) && al16(g) && al16(stats) && al16(dv) && al16(dw_partial)) {
-    e = launch_tile_bwd(p.c, p.grid, p.cpt, dtype, v, w, w_dtype, g, stats, dv, dw_partial, st);
+  if (p.kind != kPlanGeneric && al16(v) && al16(g) && al16(stats) && al16(dv) &&
+      al16(dw_partial)) {
+    e = launch_plan_bwd(p, dtype, v, w, w_dtype, g, stats, dv, dw_partial, st);
     return cuda_status(e, "sy_bwd: tile kernel launch");
   }
   if (N > kGenericMaxN || (N * 8 + 3 * N) * 4 > di.max_smem) return SY_ERR_UNSUPPORTED;
@@ -284,7 +387,7 @@ int sy_speed_of_light(const void* v, void* out, int64_t N, int64_t BT, int64_t D
   if (e != cudaSuccess) return cuda_status(e, "sy_speed_of_light: device query");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const TilePlan p = plan_tile(kOpSol, N, BT, D, dtype, di);
-  if (p.ok && al16(v) && al16(out)) {
+  if (p.kind != kPlanGeneric && al16(v) && al16(out)) {
     e = launch_tile_sol(p.c, p.grid, p.cpt, dtype, v, out, st);
     return cuda_status(e, "sy_speed_of_light: tile kernel launch");
   }
@@ -292,24 +395,39 @@ int sy_speed_of_light(const void* v, void* out, int64_t N, int64_t BT, int64_t D
   return cuda_status(e, "sy_speed_of_light: generic kernel launch");
 }
 
-int sy_plan_kind(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype) {
-  if (!esize_of(dtype)) return -SY_ERR_DTYPE;
-  if (N < 1 || BT < 0 || D < 0) return -SY_ERR_ARG;
+int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype, int sms,
+                 int max_smem, int64_t* out) {
+  if (!out) return SY_ERR_ARG;
+  if (!esize_of(dtype)) return SY_ERR_DTYPE;
+  if (N < 1 || BT < 0 || D < 0 || op < 0 || op > 3) return SY_ERR_ARG;
   DevInfo di;
-  if (dev_info(&di) != cudaSuccess) return -SY_ERR_CUDA;
-  const int64_t bt = BT < 1 ? 1 : BT;
-  switch (op) {
-    case 0:
-      return plan_tile(kOpFwd, N, bt, D, dtype, di).ok ? 1 : 0;
-    case 1:
-      return plan_tile(kOpBwd, N, bt, D, dtype, di).ok ? 1 : 0;
-    case 2:
-      if (S < 1) return -SY_ERR_ARG;
-      if (S == 1) return plan_tile(kOpFwd, N, bt, D, dtype, di).ok ? 1 : 0;
-      return 0;
-    default:
-      return -SY_ERR_ARG;
+  if (sms > 0 && max_smem > 0) {
+    di.sms = sms;
+    di.max_smem = max_smem;
+  } else {
+    const cudaError_t e = dev_info(&di);
+    if (e != cudaSuccess) return cuda_status(e, "sy_plan_info: device query");
   }
+  const int64_t bt = BT < 1 ? 1 : BT;
+  int top = op == 1 ? kOpBwd : (op == 3 ? kOpSol : kOpFwd);
+  if (op == 2 && S < 1) return SY_ERR_ARG;
+  TilePlan p;
+  if (op != 2 || S == 1) p = plan_tile(top, N, bt, D, dtype, di);
+  out[0] = p.kind;
+  out[1] = p.grid;
+  out[2] = p.c.stages;
+  out[3] = p.c.groups;
+  out[4] = p.c.tg;
+  out[5] = p.cpt;
+  out[6] = p.c.stage_bytes;
+  out[7] = p.smem;
+  return SY_OK;
+}
+
+int sy_plan_kind(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype) {
+  int64_t info[8];
+  const int st = sy_plan_info(op, N, BT, D, S, dtype, 0, 0, info);
+  return st == SY_OK ? (int)info[0] : -st;
 }
 
 int sy_device_error(int* code) {

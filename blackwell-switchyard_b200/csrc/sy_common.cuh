@@ -199,17 +199,30 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   }
 }
 
+#ifndef SY_TUNE_L2HINT
+#define SY_TUNE_L2HINT 1
+#endif
+
 // Global -> shared bulk copy (no tensor map; both addresses 16-byte aligned,
 // size a multiple of 16). Completion is signalled as transaction bytes on
 // `bar`. The L2 policy marks the source evict-first: every byte of v is read
 // exactly once per call.
 __device__ __forceinline__ void bulk_g2s(void* smem_dst, const void* gsrc, uint32_t bytes,
                                          uint64_t* bar, uint64_t policy) {
+#if SY_TUNE_L2HINT
   asm volatile(
       "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint "
       "[%0], [%1], %2, [%3], %4;" ::"r"(smem_u32(smem_dst)),
       "l"(gsrc), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
       : "memory");
+#else
+  (void)policy;
+  asm volatile(
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gsrc), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+#endif
 }
 
 __device__ __forceinline__ uint64_t policy_evict_first() {

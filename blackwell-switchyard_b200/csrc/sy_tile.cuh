@@ -75,6 +75,19 @@ cudaError_t launch_tile_bwd(const TileCfg& c, int grid, int cpt, int dtype, cons
                             const void* w, int w_dtype, const void* g, const float* stats,
                             void* dv, float* dw_partial, cudaStream_t st);
 
+// Register-tile kernels (sy_reg_{bf16,f16,f32}.cu), exact N in 1..16.
+#define SY_REG_DECL(dt)                                                                         \
+  cudaError_t launch_reg_fwd_##dt(const TileCfg& c, int grid, int cpt, const void* v,          \
+                                  const void* w, int w_dtype, void* out, float* stats,          \
+                                  cudaStream_t st);                                             \
+  cudaError_t launch_reg_bwd_##dt(const TileCfg& c, int grid, int cpt, const void* v,          \
+                                  const void* w, int w_dtype, const void* g, const float* stats, \
+                                  void* dv, float* dwp, cudaStream_t st);
+SY_REG_DECL(bf16)
+SY_REG_DECL(f16)
+SY_REG_DECL(f32)
+#undef SY_REG_DECL
+
 // Generic kernels (sy_generic.cu): any D, any 2-byte/4-byte alignment, N up to
 // kGenericMaxN. One CTA per token, two passes over the row (second from L2).
 constexpr int kGenericMaxN = 2048;

@@ -47,6 +47,12 @@ __global__ void __launch_bounds__(32 + kConsumerThreads, 1)
   const int nwc = c.groups * wpg;
   const int N = c.N;
 
+  // The stage/group protocol needs S % G == 0 (see the planner); refuse any
+  // other plan instead of running it.
+  if (c.groups < 1 || c.stages % c.groups != 0) {
+    if (tid == 0) record_device_error(kDevErrBadPlan);
+    return;
+  }
   if (tid == 0) {
     for (int s = 0; s < c.stages; ++s) {
       mbar_init(&full[s], 1);
@@ -284,9 +290,10 @@ cudaError_t launch_tile_bwd(const TileCfg& c, int grid, int cpt, int dtype, cons
 }
 
 // ---------------------------------------------------------------------------
-// dw[d] = sum_p part[p, d]. A CTA owns 32 consecutive columns; its 8 warps
-// each sum the rows p = warp, warp+8, ... in increasing order, then warp 0
-// adds the 8 slice sums in slice order. Fixed order => deterministic.
+// dw[d] = sum_p part[p, d]. A CTA owns 32 consecutive columns; warp k of its 8
+// sums rows p = k, k+8, k+16, ... in increasing order, eight loads in flight
+// at a time (one fixed-order chain), then warp 0 adds the 8 warp sums in warp
+// order. Fixed order everywhere => deterministic.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict__ part, long long P,
                                                         long long D, void* __restrict__ dw,
@@ -297,8 +304,17 @@ __global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict_
   const int wp = threadIdx.x >> 5;
   const long long col = (long long)blockIdx.x * 32 + lane;
   float acc = 0.f;
-  if (col < D)
-    for (long long p = wp; p < P; p += 8) acc += part[p * D + col];
+  if (col < D) {
+    long long p = wp;
+    for (; p + 56 < P; p += 64) {
+      float x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) x[i] = __ldcs(part + (p + 8 * i) * D + col);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc += x[i];
+    }
+    for (; p < P; p += 8) acc += __ldcs(part + p * D + col);
+  }
   slice[wp][lane] = acc;
   __syncthreads();
   if (wp == 0 && col < D) {

@@ -41,6 +41,12 @@ __global__ void __launch_bounds__(32 + kConsumerThreads, 1)
   const int wpg = c.tg >> 5;  // warps per consumer group
   const int nwc = c.groups * wpg;
 
+  // The stage/group protocol needs S % G == 0 (see the planner); refuse any
+  // other plan instead of running it.
+  if (c.groups < 1 || c.stages % c.groups != 0) {
+    if (tid == 0) record_device_error(kDevErrBadPlan);
+    return;
+  }
   if (tid == 0) {
     for (int s = 0; s < c.stages; ++s) {
       mbar_init(&full[s], 1);

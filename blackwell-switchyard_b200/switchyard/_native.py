@@ -38,6 +38,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sy_fwd_batched": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I, _F, _P], _I),
     "sy_speed_of_light": ([_P, _P, _I64, _I64, _I64, _I, _P], _I),
     "sy_plan_kind": ([_I, _I64, _I64, _I64, _I64, _I], _I),
+    "sy_plan_info": ([_I, _I64, _I64, _I64, _I64, _I, _I, _I, _c.POINTER(_I64)], _I),
     "sy_device_error": ([_c.POINTER(_c.c_int)], _I),
 }
 
@@ -153,6 +154,18 @@ def speed_of_light(v, out, n, bt, d) -> None:
 
 def plan_kind(op: int, n: int, bt: int, d: int, s: int, dtype: torch.dtype) -> int:
     return int(lib.sy_plan_kind(op, n, bt, d, s, dtype_code(dtype)))
+
+
+PLAN_FIELDS = ("kind", "grid", "stages", "groups", "threads_per_group", "chunks_per_thread",
+               "stage_bytes", "smem_bytes")
+
+
+def plan_info(op: int, n: int, bt: int, d: int, s: int, dtype: torch.dtype, sms: int = 0,
+              max_smem: int = 0) -> dict:
+    """The launch plan for a shape (on the current device unless sms/max_smem given)."""
+    out = (_I64 * 8)()
+    check(lib.sy_plan_info(op, n, bt, d, s, dtype_code(dtype), sms, max_smem, out), "sy_plan_info")
+    return dict(zip(PLAN_FIELDS, (int(x) for x in out)))
 
 
 def device_error() -> int:

@@ -129,18 +129,32 @@ SY_API int sy_speed_of_light(const void* v, void* out, int64_t N, int64_t BT,
 
 /*
  * Which kernel family sy_fwd / sy_bwd / sy_fwd_batched would launch for a
- * shape, without launching: 1 = TMA-pipelined tile kernel, 2 = cluster
- * D-split tile kernel, 0 = generic (any stride/size) kernel, <0 = error.
- * `op` is 0 forward, 1 backward, 2 batched (S queries). Used by tests to pin
- * dispatch, like the reference's _launch_config tests.
+ * shape on the current device, without launching: 1 = register-tile kernel
+ * (exact N, TMA-pipelined), 2 = shared-memory tile kernel (run-time N,
+ * TMA-pipelined), 0 = generic (any size/alignment) kernel, <0 = -status.
+ * `op` is 0 forward, 1 backward, 2 batched (S queries), 3 speed of light.
+ * Used by tests to pin dispatch, like the reference's _launch_config tests
+ * (src/switchyard/triton_op.py:130-150, :267-276, :420-435).
  */
 SY_API int sy_plan_kind(int op, int64_t N, int64_t BT, int64_t D, int64_t S,
-                 int dtype);
+                        int dtype);
 
 /*
- * Reads the device-side error word of the current device (set when a
- * kernel's bounded wait ran out) and clears it. Synchronises the device.
- * Writes 0 to *code when no error was recorded.
+ * The full launch plan for a shape on a device with `sms` multiprocessors
+ * and `max_smem` bytes of opt-in shared memory per block (pass 0, 0 for the
+ * current device). Writes out[8] = {kind (as sy_plan_kind), grid, pipeline
+ * stages, consumer groups, threads per group, 16-byte chunks per thread per
+ * row, bytes per stage, dynamic shared memory bytes}. No reference
+ * counterpart; exposes the planner to tests.
+ */
+SY_API int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S,
+                        int dtype, int sms, int max_smem, int64_t* out);
+
+/*
+ * Reads the device-side error word of the current device and clears it.
+ * Synchronises the device. Bit 1: a kernel's bounded wait ran out; bit 2: a
+ * kernel refused an inconsistent launch plan. Writes 0 to *code when no error
+ * was recorded.
  */
 SY_API int sy_device_error(int* code);
 

@@ -82,3 +82,40 @@ def test_host_validation_rejects_bad_arguments(native):
     assert L.sy_dw_reduce(None, 1, 0, None, bf16, None) == native.SY_OK
     assert L.sy_bwd_partials(3, 0, 16, bf16) == 1
     assert L.sy_bwd_partials(0, 4, 16, bf16) < 0
+
+
+B200 = dict(sms=148, max_smem=232448)  # multiprocessors, opt-in shared memory per block
+
+
+@pytest.mark.parametrize("dtype_name", ["bfloat16", "float16", "float32"])
+def test_planner_invariants_for_b200(native, dtype_name):
+    """Every tile plan fits the device and keeps the pipeline's invariants:
+    at least two stages, groups within the 256 consumer threads, the
+    shared-memory tile's stage count a multiple of its group count (its
+    parity protocol needs it), and the representative shape on the
+    register-tile kernels. Pure host logic: no GPU needed."""
+    import torch
+
+    dt = getattr(torch, dtype_name)
+    for n in (1, 2, 3, 5, 8, 9, 10, 16, 17, 33, 64):
+        for d in (64, 320, 512, 1024, 1536, 2048, 4096, 8192):
+            for op in (0, 1):
+                p = native.plan_info(op, n, 4096, d, 1, dt, **B200)
+                if p["kind"] == 0:
+                    continue
+                assert p["smem_bytes"] <= B200["max_smem"]
+                assert p["stages"] >= 2 and p["groups"] >= 1
+                assert p["groups"] * p["threads_per_group"] <= 256
+                assert p["threads_per_group"] % 32 == 0
+                assert p["grid"] == 148
+                assert p["chunks_per_thread"] * p["threads_per_group"] * 16 >= d * dt.itemsize
+                if p["kind"] == 2:
+                    assert p["stages"] % p["groups"] == 0
+                    assert n <= 64
+                if p["kind"] == 1:
+                    assert n <= 16
+    rep = native.plan_info(0, 9, 4096, 2048, 1, torch.bfloat16, **B200)
+    assert rep["kind"] == 1 and rep["stages"] >= 4
+    assert native.plan_info(1, 9, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 1
+    # rows that are not a multiple of 16 bytes go to the generic kernels
+    assert native.plan_info(0, 3, 64, 777, 1, torch.bfloat16, **B200)["kind"] == 0
