@@ -8,6 +8,7 @@
 #include <mutex>
 
 #include "sy_reg.cuh"
+#include "sy_stream.cuh"
 #include "sy_tile.cuh"
 
 // Planner tuning knobs. The defaults are the shipped configuration; builds
@@ -20,6 +21,9 @@
 #endif
 #ifndef SY_TUNE_CTAS_PER_SM
 #define SY_TUNE_CTAS_PER_SM 1
+#endif
+#ifndef SY_TUNE_PDL
+#define SY_TUNE_PDL 1  // launch the dw reduction as a programmatic dependent
 #endif
 
 namespace sy {
@@ -73,7 +77,7 @@ bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 int64_t stats_stride(int64_t N) { return ((2 * N + 2) + 3) / 4 * 4; }
 
 enum TileOp { kOpFwd = 0, kOpBwd = 1, kOpSol = 2 };
-enum PlanKind { kPlanGeneric = 0, kPlanRegTile = 1, kPlanSmemTile = 2 };
+enum PlanKind { kPlanGeneric = 0, kPlanRegTile = 1, kPlanSmemTile = 2, kPlanStream = 3 };
 
 struct TilePlan {
   int kind = kPlanGeneric;
@@ -144,18 +148,26 @@ TilePlan plan_tile(int op, int64_t N, int64_t BT, int64_t D, int dtype, const De
 
   // 1) register tile: exact-N kernels, the packed tile (N * CPT * 4 words)
   //    held in registers; two chunks per thread up to N = 9, else one.
-  if (op != kOpSol && N <= kRegMaxN) {
+  if (op != kOpSol && N <= (op == kOpFwd ? kRegFwdMaxN : kRegMaxN)) {
+    // Chunks per thread: the more, the fewer warps share a token, so the
+    // per-warp cost of its reductions and softmax is spread over more data
+    // and more tokens are in flight per SM. Forward: up to 4 (N <= 9; the tile
+    // is then kept packed), backward: up to 2 (N <= 9, more live state).
+    // Never so many that a warp's lanes would sit idle.
     int cpt = 0, tg = 0;
-    if (N <= kRegMaxN2) {
-      const int64_t t = round32((rc + 1) / 2);
-      if (t <= kConsumerThreads && (rc + t - 1) / t <= 2) cpt = 2, tg = (int)t;
+    const int max_cpt = N <= kRegMaxN4 && op == kOpFwd ? 4 : (N <= kRegMaxN2 ? 2 : 1);
+    for (int cand = max_cpt; cand >= 1 && !cpt; cand /= 2) {
+      if (cand > 1 && rc < 32 * cand) continue;  // lanes would be idle
+      const int64_t t = round32((rc + cand - 1) / cand);
+      if (t <= 256 && (rc + t - 1) / t <= cand) cpt = cand, tg = (int)t;
     }
-    if (!cpt && round32(rc) <= kConsumerThreads) cpt = 1, tg = (int)round32(rc);
     if (cpt) {
       TileCfg rcfg = c;
       rcfg.tg = tg;
-      rcfg.coef_stride = 0;
-      int groups = kConsumerThreads / tg;
+      rcfg.coef_stride = op == kOpBwd ? tile_coef_stride((int)N) : 0;  // bwd: float4 per source
+      rcfg.w_smem = op == kOpBwd ? 0 : 1;  // forward reads its fp32 w from shared memory
+      int groups = reg_threads((int)N, cpt, op == kOpBwd) / tg;
+      if (groups > 16) groups = 16;  // named barrier ids 1..15 (1-warp groups use none)
       if (SY_TUNE_GROUPS > 0) groups = SY_TUNE_GROUPS;
       if (size_ring(rcfg, op, groups < 1 ? 1 : groups, di, &p.smem, /*per_group_rings=*/true)) {
         p.kind = kPlanRegTile;
@@ -189,6 +201,50 @@ TilePlan plan_tile(int op, int64_t N, int64_t BT, int64_t D, int dtype, const De
   p.c = c;
   p.cpt = cpt;
   p.grid = grid;
+  return p;
+}
+
+struct StreamPlan {
+  bool ok = false;
+  StreamCfg c{};
+  int grid = 0;
+  int cpl = 0;
+  int64_t smem = 0;
+};
+
+// Row-stream forward (one warp per token, online softmax): rows must be a
+// multiple of 16 bytes and fit 8 16-byte chunks per lane (bf16/f16 D <= 2048,
+// fp32 D <= 1024); any N.
+StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInfo& di) {
+  StreamPlan p;
+  const int es = esize_of(dtype);
+  if (!es || N < 1 || D < 1 || D > kMaxD || BT < 1 || BT > INT_MAX) return p;
+  if ((D * es) % 16) return p;
+  const int64_t rc = D * es / 16;
+  int cpl = 1;
+  while (cpl * 32 < rc) cpl *= 2;
+  if (cpl > 8) return p;
+  StreamCfg c{};
+  c.BT = BT;
+  c.N = (int)N;
+  c.D = (int)D;
+  c.row_chunks = (int)rc;
+  c.row_bytes = (int)(D * es);
+  c.warps = stream_threads(cpl) / 32;
+  c.stats_stride = (int)stats_stride(N);
+  c.ring = 0;
+  const int64_t fixed = (int64_t)stream_smem_layout(c).total;
+  int64_t ring = (di.max_smem - fixed) / ((int64_t)c.warps * (c.row_bytes + 8));
+  if (ring > 8) ring = 8;
+  if (ring < 2) return p;
+  c.ring = (int)ring;
+  p.smem = (int64_t)stream_smem_layout(c).total;
+  if (p.smem > di.max_smem) return p;
+  const int64_t need = (BT + c.warps - 1) / c.warps;  // CTAs with work for every warp
+  p.grid = (int)(need < di.sms ? need : di.sms);
+  p.c = c;
+  p.cpl = cpl;
+  p.ok = true;
   return p;
 }
 
@@ -293,8 +349,18 @@ int sy_fwd(const void* v, const void* w, void* out, float* stats, int64_t N, int
   cudaError_t e = dev_info(&di);
   if (e != cudaSuccess) return cuda_status(e, "sy_fwd: device query");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool aligned = al16(v) && al16(out);
   const TilePlan p = plan_tile(kOpFwd, N, BT, D, dtype, di);
-  if (p.kind != kPlanGeneric && al16(v) && al16(out)) {
+  if (p.kind == kPlanRegTile && aligned) {
+    e = launch_plan_fwd(p, dtype, v, w, w_dtype, out, stats, st);
+    return cuda_status(e, "sy_fwd: register-tile kernel launch");
+  }
+  const StreamPlan sp = plan_stream(N, BT, D, dtype, di);
+  if (sp.ok && aligned) {
+    e = launch_stream_fwd(sp.c, sp.grid, sp.cpl, dtype, v, w, w_dtype, out, stats, false, st);
+    return cuda_status(e, "sy_fwd: stream kernel launch");
+  }
+  if (p.kind != kPlanGeneric && aligned) {
     e = launch_plan_fwd(p, dtype, v, w, w_dtype, out, stats, st);
     return cuda_status(e, "sy_fwd: tile kernel launch");
   }
@@ -354,7 +420,8 @@ int sy_dw_reduce(const float* dw_partial, int64_t P, int64_t D, void* dw, int dw
   if (!dw_partial || !dw) return SY_ERR_ARG;
   if (D > kMaxD) return SY_ERR_UNSUPPORTED;
   const cudaError_t e =
-      launch_dw_reduce(dw_partial, P, D, dw, dw_dtype, true, static_cast<cudaStream_t>(stream));
+      launch_dw_reduce(dw_partial, P, D, dw, dw_dtype, SY_TUNE_PDL != 0,
+                       static_cast<cudaStream_t>(stream));
   return cuda_status(e, "sy_dw_reduce: launch");
 }
 
@@ -386,6 +453,11 @@ int sy_speed_of_light(const void* v, void* out, int64_t N, int64_t BT, int64_t D
   cudaError_t e = dev_info(&di);
   if (e != cudaSuccess) return cuda_status(e, "sy_speed_of_light: device query");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const StreamPlan sp = plan_stream(N, BT, D, dtype, di);
+  if (sp.ok && al16(v) && al16(out)) {
+    e = launch_stream_fwd(sp.c, sp.grid, sp.cpl, dtype, v, nullptr, SY_F32, out, nullptr, true, st);
+    return cuda_status(e, "sy_speed_of_light: stream kernel launch");
+  }
   const TilePlan p = plan_tile(kOpSol, N, BT, D, dtype, di);
   if (p.kind != kPlanGeneric && al16(v) && al16(out)) {
     e = launch_tile_sol(p.c, p.grid, p.cpt, dtype, v, out, st);
@@ -411,6 +483,22 @@ int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype,
   const int64_t bt = BT < 1 ? 1 : BT;
   int top = op == 1 ? kOpBwd : (op == 3 ? kOpSol : kOpFwd);
   if (op == 2 && S < 1) return SY_ERR_ARG;
+  if (top != kOpBwd && (op != 2 || S == 1)) {
+    const StreamPlan sp = plan_stream(N, bt, D, dtype, di);
+    const bool reg_first =
+        top == kOpFwd && plan_tile(kOpFwd, N, bt, D, dtype, di).kind == kPlanRegTile;
+    if (sp.ok && !reg_first) {
+      out[0] = kPlanStream;
+      out[1] = sp.grid;
+      out[2] = sp.c.ring;
+      out[3] = sp.c.warps;
+      out[4] = 32;
+      out[5] = sp.cpl;
+      out[6] = sp.c.row_bytes;
+      out[7] = sp.smem;
+      return SY_OK;
+    }
+  }
   TilePlan p;
   if (op != 2 || S == 1) p = plan_tile(top, N, bt, D, dtype, di);
   out[0] = p.kind;

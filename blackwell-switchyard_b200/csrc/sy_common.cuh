@@ -237,10 +237,42 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
+// Order this thread's (and, through a preceding barrier, its group's)
+// generic-proxy reads of shared memory before async-proxy (bulk copy) writes
+// to the same bytes.
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Named barrier over `nthreads` threads (a multiple of 32). id 0 is
 // __syncthreads; the kernels use 1..15.
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// packed fp32 helpers (float2 = one fma.rn.f32x2 lane pair)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+
+// Unpack one 16-byte chunk into VEC/2 float2 pairs (elements 2i, 2i+1).
+template <typename T>
+__device__ __forceinline__ void unpack2(const uint4& u, float2* p) {
+  float x[Dt<T>::kVec];
+  Dt<T>::unpack(u, x);
+#pragma unroll
+  for (int i = 0; i < Dt<T>::kVec / 2; ++i) p[i] = make_float2(x[2 * i], x[2 * i + 1]);
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 pack2(const float2* p) {
+  float x[Dt<T>::kVec];
+#pragma unroll
+  for (int i = 0; i < Dt<T>::kVec / 2; ++i) {
+    x[2 * i] = p[i].x;
+    x[2 * i + 1] = p[i].y;
+  }
+  return Dt<T>::pack(x);
 }
 
 // ---------------------------------------------------------------------------

@@ -30,32 +30,48 @@ namespace sy {
 
 extern __shared__ __align__(1024) unsigned char sy_smem[];
 
-// Largest N with a register-tile instantiation, and with a two-chunk one
-// (the packed tile is N * CPT * 4 registers per thread).
+// Largest N with a register-tile instantiation, and with two- and
+// four-chunk ones (the packed tile is N * CPT * 4 registers per thread).
 constexpr int kRegMaxN = 16;
-constexpr int kRegMaxN2 = 9;
+constexpr int kRegMaxN2 = 9;   // two chunks per thread up to this N
+constexpr int kRegMaxN4 = 6;   // forward: four chunks per thread up to this N
+constexpr int kRegFwdMaxN = 9; // forward: larger N takes the row-stream kernel
 
-__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+#ifndef SY_TUNE_REG_FWD_THREADS
+#define SY_TUNE_REG_FWD_THREADS 256
+#endif
+#ifndef SY_TUNE_REG_BWD_THREADS
+#define SY_TUNE_REG_BWD_THREADS 256
+#endif
 
-// Unpack one 16-byte chunk into VEC/2 float2 pairs (elements 2i, 2i+1).
-template <typename T>
-__device__ __forceinline__ void unpack2(const uint4& u, float2* p) {
-  float x[Dt<T>::kVec];
-  Dt<T>::unpack(u, x);
-#pragma unroll
-  for (int i = 0; i < Dt<T>::kVec / 2; ++i) p[i] = make_float2(x[2 * i], x[2 * i + 1]);
+// Threads per CTA of a register-tile instantiation (the launch bound that sets
+// the register budget): 256, i.e. up to 255 registers per thread -- room for
+// the forward's unpacked fp32 tile (N * CPT * VEC floats, 144 at N=9 bf16).
+__host__ __device__ constexpr int reg_threads(int /*n*/, int /*cpt*/, bool bwd) {
+  return bwd ? SY_TUNE_REG_BWD_THREADS : SY_TUNE_REG_FWD_THREADS;
 }
 
-template <typename T>
-__device__ __forceinline__ uint4 pack2(const float2* p) {
-  float x[Dt<T>::kVec];
+// A token's register tile: N rows x CPT chunks, held either as fp32 pairs
+// (unpacked once at load) or as the raw 16-byte words (unpacked at each use).
+template <typename T, int N, int CPT, bool PACKED>
+struct Tile;
+
+template <typename T, int N, int CPT>
+struct Tile<T, N, CPT, false> {
+  float2 f[N][CPT][Dt<T>::kVec / 2];
+  __device__ __forceinline__ void load(int n, int cc, const uint4& u) { unpack2<T>(u, f[n][cc]); }
+  __device__ __forceinline__ void get(int n, int cc, float2* p) const {
 #pragma unroll
-  for (int i = 0; i < Dt<T>::kVec / 2; ++i) {
-    x[2 * i] = p[i].x;
-    x[2 * i + 1] = p[i].y;
+    for (int i = 0; i < Dt<T>::kVec / 2; ++i) p[i] = f[n][cc][i];
   }
-  return Dt<T>::pack(x);
-}
+};
+
+template <typename T, int N, int CPT>
+struct Tile<T, N, CPT, true> {
+  uint4 u[N][CPT];
+  __device__ __forceinline__ void load(int n, int cc, const uint4& w) { u[n][cc] = w; }
+  __device__ __forceinline__ void get(int n, int cc, float2* p) const { unpack2<T>(u[n][cc], p); }
+};
 
 // Sum M (16 or 32) per-lane values over the warp. Afterwards lane L holds the
 // warp total of value (L >> (5 - log2 M)); for M == 32 that is value L, for
@@ -156,17 +172,11 @@ __device__ __forceinline__ void issue_token(unsigned char* dst, uint64_t* bar, c
   }
 }
 
-// Order the group's generic-proxy reads of a stage (made visible to this
-// thread by the group barrier) before the async-proxy writes that refill it.
-__device__ __forceinline__ void fence_proxy_async() {
-  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-}
-
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
 template <typename T, int N, int CPT>
-__global__ void __launch_bounds__(kConsumerThreads, 1)
+__global__ void __launch_bounds__(reg_threads(N, CPT, false), 1)
     reg_fwd_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
                    T* __restrict__ out, float* __restrict__ stats, const TileCfg c) {
   constexpr int VEC = Dt<T>::kVec;
@@ -177,6 +187,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1)
   unsigned char* stage0 = sy_smem + L.stages_off;
   float* red_base = reinterpret_cast<float*>(sy_smem + L.red_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(sy_smem + L.bar_off);
+  const unsigned char* zero_pad = sy_smem + L.zero_off;
 
   const int tid = threadIdx.x;
   const int lane = tid & 31;
@@ -186,13 +197,20 @@ __global__ void __launch_bounds__(kConsumerThreads, 1)
   const int wpg = c.tg >> 5;
   const int nwc = c.groups * wpg;
 
-  if (c.N != N || c.groups < 1 || c.stages < c.groups || c.red_stride < M) {
+  if (c.N != N || c.groups < 1 || c.stages < c.groups || c.red_stride < M || !c.w_smem) {
     if (tid == 0) record_device_error(kDevErrBadPlan);
     return;
   }
   if (tid == 0) {
     for (int s = 0; s < c.stages; ++s) mbar_init(&full[s], 1);
+    *reinterpret_cast<uint4*>(sy_smem + L.zero_off) = make_uint4(0u, 0u, 0u, 0u);
     mbar_fence_init();
+  }
+  // fp32 w in 16-byte planes: plane q of chunk ch holds w[ch*VEC + 4q .. 4q+3]
+  float* wsm = reinterpret_cast<float*>(sy_smem + L.w_off);
+  for (int d = tid; d < c.D; d += blockDim.x) {
+    const int ch = d / VEC, e = d - ch * VEC;
+    wsm[((e >> 2) * c.row_chunks + ch) * 4 + (e & 3)] = load_any(w, w_dtype, d);
   }
   __syncthreads();
 
@@ -215,17 +233,8 @@ __global__ void __launch_bounds__(kConsumerThreads, 1)
                   nullptr, 0, pol);
 
   bool cv[CPT];
-  float2 w2[CPT][P];
 #pragma unroll
-  for (int cc = 0; cc < CPT; ++cc) {
-    const int chunk = tig + cc * c.tg;
-    cv[cc] = chunk < c.row_chunks;
-#pragma unroll
-    for (int i = 0; i < P; ++i)
-      w2[cc][i] = cv[cc] ? make_float2(load_any(w, w_dtype, (long long)chunk * VEC + 2 * i),
-                                       load_any(w, w_dtype, (long long)chunk * VEC + 2 * i + 1))
-                         : make_float2(0.f, 0.f);
-  }
+  for (int cc = 0; cc < CPT; ++cc) cv[cc] = tig + cc * c.tg < c.row_chunks;
   const float inv_d = 1.f / (float)c.D;
 
   int slot = 0;
@@ -235,32 +244,57 @@ __global__ void __launch_bounds__(kConsumerThreads, 1)
     if (!mbar_wait(&full[sidx], ph)) return;
     const unsigned char* tile = stage0 + (size_t)sidx * c.stage_bytes;
     const long long tok = cta + (long long)(g + j * c.groups) * grid;
-    // ---- registers <- stage; phase A on the registers ----
-    uint4 x[N][CPT];
+    // ---- registers <- stage (unpacked once to fp32); phase A ----
+    // A chunk past the end of the row reads the 16-byte zero pad instead
+    // (stride 0), so the loads need no predicate.
+    const unsigned char* cb[CPT];
+    int cs[CPT];
+#pragma unroll
+    for (int cc = 0; cc < CPT; ++cc) {
+      cb[cc] = cv[cc] ? tile + (tig + cc * c.tg) * 16 : zero_pad;
+      cs[cc] = cv[cc] ? c.row_bytes : 0;
+    }
+    // The tile stays packed (16-byte words) when unpacking it would not fit
+    // the register budget; it is then unpacked again in phase B.
+    constexpr bool PACKED = N * CPT * VEC > 144;
+    Tile<T, N, CPT, PACKED> x;
 #pragma unroll
     for (int n = 0; n < N; ++n)
 #pragma unroll
-      for (int cc = 0; cc < CPT; ++cc)
-        x[n][cc] = cv[cc] ? lds128(tile + (size_t)n * c.row_bytes + (tig + cc * c.tg) * 16)
-                          : make_uint4(0u, 0u, 0u, 0u);
+      for (int cc = 0; cc < CPT; ++cc) x.load(n, cc, lds128(cb[cc] + n * cs[cc]));
+    // chunk-outer: the chunk's w (fp32, from shared memory) is read once and
+    // every row accumulates into its own dot / sum-of-squares pair
+    float2 dot2[N], ssq2[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) dot2[n] = ssq2[n] = make_float2(0.f, 0.f);
+#pragma unroll
+    for (int cc = 0; cc < CPT; ++cc) {
+      float2 wv[P];
+      const float4* wp = reinterpret_cast<const float4*>(wsm) + (tig + cc * c.tg);
+#pragma unroll
+      for (int i = 0; i < P; i += 2) {
+        const float4 q = cv[cc] ? wp[(i / 2) * c.row_chunks] : make_float4(0.f, 0.f, 0.f, 0.f);
+        wv[i] = make_float2(q.x, q.y);
+        wv[i + 1] = make_float2(q.z, q.w);
+      }
+#pragma unroll
+      for (int n = 0; n < N; ++n) {
+        float2 p[P];
+        x.get(n, cc, p);
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+          dot2[n] = __ffma2_rn(wv[i], p[i], dot2[n]);
+          ssq2[n] = __ffma2_rn(p[i], p[i], ssq2[n]);
+        }
+      }
+    }
     float a[M];
 #pragma unroll
     for (int i = 0; i < M; ++i) a[i] = 0.f;
 #pragma unroll
     for (int n = 0; n < N; ++n) {
-      float2 dot = make_float2(0.f, 0.f), ssq = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int cc = 0; cc < CPT; ++cc) {
-        float2 p[P];
-        unpack2<T>(x[n][cc], p);
-#pragma unroll
-        for (int i = 0; i < P; ++i) {
-          dot = __ffma2_rn(w2[cc][i], p[i], dot);
-          ssq = __ffma2_rn(p[i], p[i], ssq);
-        }
-      }
-      a[n] = dot.x + dot.y;
-      a[HALF + n] = ssq.x + ssq.y;
+      a[n] = dot2[n].x + dot2[n].y;
+      a[HALF + n] = ssq2[n].x + ssq2[n].y;
     }
     // ---- cross-thread reduction ----
     const float tot_l = warp_reduce_scatter<M>(a, lane);
@@ -317,7 +351,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1)
 #pragma unroll
       for (int n = 0; n < N; ++n) {
         float2 p[P];
-        unpack2<T>(x[n][cc], p);
+        x.get(n, cc, p);
 #pragma unroll
         for (int i = 0; i < P; ++i) o[i] = __ffma2_rn(f2(al[n]), p[i], o[i]);
       }
@@ -336,7 +370,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1)
 // backward (see sy_tile_bwd.cu for the formulas)
 // ---------------------------------------------------------------------------
 template <typename T, int N, int CPT>
-__global__ void __launch_bounds__(kConsumerThreads, 1)
+__global__ void __launch_bounds__(reg_threads(N, CPT, true), 1)
     reg_bwd_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
                    const T* __restrict__ gin, const float* __restrict__ stats, T* __restrict__ dv,
                    float* __restrict__ dw_partial, const TileCfg c) {
@@ -346,6 +380,7 @@ __global__ void __launch_bounds__(kConsumerThreads, 1)
   const TileSmem L = tile_smem_layout(c);
   unsigned char* stage0 = sy_smem + L.stages_off;
   float* red_base = reinterpret_cast<float*>(sy_smem + L.red_off);
+  float* coef_base = reinterpret_cast<float*>(sy_smem + L.coef_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(sy_smem + L.bar_off);
 
   const int tid = threadIdx.x;
@@ -356,7 +391,8 @@ __global__ void __launch_bounds__(kConsumerThreads, 1)
   const int wpg = c.tg >> 5;
   const int nwc = c.groups * wpg;
 
-  if (c.N != N || c.groups < 1 || c.stages < c.groups || c.red_stride < M) {
+  if (c.N != N || c.groups < 1 || c.stages < c.groups || c.red_stride < M ||
+      c.coef_stride < 4 * N) {
     if (tid == 0) record_device_error(kDevErrBadPlan);
     return;
   }
@@ -470,13 +506,12 @@ __global__ void __launch_bounds__(kConsumerThreads, 1)
     const float dl = alpha * (Gn - S);
     const float da_l = dl * r;
     const float cv_l = -dl * logit * r * r * inv_d;
-    float al[N], da[N], cf[N];
-#pragma unroll
-    for (int n = 0; n < N; ++n) {
-      al[n] = __shfl_sync(kFull, alpha, n);
-      da[n] = __shfl_sync(kFull, da_l, n);
-      cf[n] = __shfl_sync(kFull, cv_l, n);
-    }
+    // The warp's coefficients go to its own slot of shared memory and are
+    // read back with broadcast loads (cheaper in registers than 3N shuffles).
+    float4* coef = reinterpret_cast<float4*>(coef_base + (size_t)cw * c.coef_stride);
+    __syncwarp();  // the previous token's phase B reads of coef are done
+    if (lane < N) coef[lane] = make_float4(alpha, da_l, cv_l, 0.f);
+    __syncwarp();
 
     // ---- phase B: dv_n = alpha_n g + da_n w + cv_n v_n ; dw += da_n v_n ----
 #pragma unroll
@@ -487,13 +522,13 @@ __global__ void __launch_bounds__(kConsumerThreads, 1)
       T* dcol = dv + (size_t)tok * c.D + (size_t)(tig + cc * c.tg) * VEC;
 #pragma unroll
       for (int n = 0; n < N; ++n) {
+        const float4 k = coef[n];  // alpha, da, cv
         float2 p[P], d[P];
         unpack2<T>(x[n][cc], p);
 #pragma unroll
         for (int i = 0; i < P; ++i) {
-          d[i] = __ffma2_rn(f2(cf[n]), p[i],
-                            __ffma2_rn(f2(da[n]), w2[cc][i], __fmul2_rn(f2(al[n]), gp[i])));
-          dw2[cc][i] = __ffma2_rn(f2(da[n]), p[i], dw2[cc][i]);
+          d[i] = __ffma2_rn(f2(k.z), p[i], __ffma2_rn(f2(k.y), w2[cc][i], __fmul2_rn(f2(k.x), gp[i])));
+          dw2[cc][i] = __ffma2_rn(f2(k.y), p[i], dw2[cc][i]);
         }
         stg128(dcol + (size_t)n * c.BT * c.D, pack2<T>(d));
       }
@@ -550,6 +585,10 @@ cudaError_t launch_reg_fwd_n(const TileCfg& c, int grid, int cpt, const void* v,
   if constexpr (N <= kRegMaxN2)
     if (cpt == 2)
       return launch_smem(reg_fwd_kernel<T, N, 2>, grid, block, smem, st, vp, w, w_dtype, op, stats,
+                         c);
+  if constexpr (N <= kRegMaxN4)
+    if (cpt == 4)
+      return launch_smem(reg_fwd_kernel<T, N, 4>, grid, block, smem, st, vp, w, w_dtype, op, stats,
                          c);
   return cudaErrorInvalidValue;
 }

@@ -1,0 +1,284 @@
+// sy_stream.cuh -- "row stream" forward: one warp per token, online softmax.
+//
+// Every warp of the persistent CTA works alone: it takes tokens
+// k = cta + grid * (warp + W * j), j = 0, 1, ... (so each SM gets an equal
+// share and, within it, its W warps take turns), and streams the token's N
+// source rows one at a time through its own ring of R shared-memory row
+// buffers, filled by cp.async.bulk (one mbarrier per buffer). Per row the
+// lane's CPL 16-byte chunks go to registers as fp32 (the buffer is refilled
+// with the row R ahead right away), then
+//
+//   dot = w.v_n, ssq = v_n.v_n         packed fp32 FMA, butterfly over the warp
+//   logit = dot * rsqrt(ssq/D + eps)    (no 1/sqrt(D); bitwise equal in all lanes)
+//   online softmax over n:             if logit > m: o = o*exp(m-logit) + v_n,
+//                                      l = l*exp(m-logit) + 1, m = logit
+//                                      else: p = exp(logit-m), o += p*v_n, l += p
+//
+// and after the last row out = o / l, rounded once. There is no block-level
+// barrier anywhere, the source count is a run-time loop (any N), and the
+// statistics (logit_n, r_n, m, lse = m + log l) fall out of the same pass.
+// w is converted to fp32 once per CTA into shared memory, stored as VEC/4
+// planes of float4 per chunk so the per-row reads are conflict-free.
+//
+// Reference math: src/switchyard/reference.py:42-59; the two-phase merge of
+// partial softmaxes it follows is reference.py:219-233 applied one row at a time.
+#pragma once
+
+#include "sy_launch.cuh"
+#include "sy_tile.cuh"
+
+namespace sy {
+
+extern __shared__ __align__(1024) unsigned char sy_smem[];
+
+struct StreamCfg {
+  long long BT;
+  int N, D;
+  int row_chunks;    // 16-byte chunks per row
+  int row_bytes;     // padded to a multiple of 16 (rows are contiguous in HBM)
+  int warps;         // W per CTA
+  int ring;          // R row buffers per warp
+  int stats_stride;
+  float eps;
+};
+
+struct StreamSmem {
+  size_t w_off, ring_off, bar_off, zero_off, total;
+};
+
+__host__ __device__ inline StreamSmem stream_smem_layout(const StreamCfg& c) {
+  StreamSmem s;
+  s.w_off = 0;                                                   // fp32 w[D]
+  s.ring_off = ((size_t)c.D * 4 + 127) / 128 * 128;              // W * R rows
+  s.bar_off = s.ring_off + (size_t)c.warps * c.ring * c.row_bytes;
+  s.zero_off = s.bar_off + (size_t)c.warps * c.ring * 8;
+  s.total = s.zero_off + 16;
+  return s;
+}
+
+#ifndef SY_TUNE_STREAM8_THREADS
+#define SY_TUNE_STREAM8_THREADS 384
+#endif
+
+// Threads per CTA for CPL chunks per lane. The fp32 row and the fp32 output
+// accumulator take 2 * 4 * CPL registers per lane (64 each at CPL=8 bf16),
+// so CPL <= 4 runs 16 warps per SM and CPL = 8 twelve (168 registers each).
+__host__ __device__ constexpr int stream_threads(int cpl) {
+  return cpl <= 4 ? 512 : SY_TUNE_STREAM8_THREADS;
+}
+
+// FULL: the row is exactly 32 * CPL chunks (D = 256, 512, 1024, 2048 bf16),
+// so no lane needs a validity predicate.
+template <typename T, int CPL, bool SOL, bool FULL>
+__global__ void __launch_bounds__(stream_threads(CPL), 1)
+    stream_fwd_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
+                      T* __restrict__ out, float* __restrict__ stats, const StreamCfg c) {
+  constexpr int VEC = Dt<T>::kVec;
+  constexpr int P = VEC / 2;
+  const StreamSmem L = stream_smem_layout(c);
+  float* wsm = reinterpret_cast<float*>(sy_smem + L.w_off);
+  unsigned char* ring0 = sy_smem + L.ring_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sy_smem + L.bar_off);
+  const unsigned char* zero_pad = sy_smem + L.zero_off;
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int wi = tid >> 5;
+  if (c.warps != (int)(blockDim.x >> 5) || c.ring < 1) {
+    if (tid == 0) record_device_error(kDevErrBadPlan);
+    return;
+  }
+
+  if (tid == 0) {
+    for (int i = 0; i < c.warps * c.ring; ++i) mbar_init(&bars[i], 1);
+    *reinterpret_cast<uint4*>(sy_smem + L.zero_off) = make_uint4(0u, 0u, 0u, 0u);
+    mbar_fence_init();
+  }
+  // plane p of chunk ch holds w[ch*VEC + 4p .. 4p+3] at wsm[(p*chunks + ch)*4]
+  if constexpr (!SOL)
+    for (int d = tid; d < c.D; d += blockDim.x) {
+      const int ch = d / VEC, e = d - ch * VEC;
+      wsm[((e >> 2) * c.row_chunks + ch) * 4 + (e & 3)] = load_any(w, w_dtype, d);
+    }
+  __syncthreads();
+
+  const long long grid = gridDim.x;
+  const long long tok0 = blockIdx.x + grid * wi;
+  const long long tstride = grid * c.warps;
+  const long long ntok = tok0 < c.BT ? (c.BT - 1 - tok0) / tstride + 1 : 0;
+  const long long nrows = ntok * c.N;  // this warp's row stream
+  unsigned char* ring = ring0 + (size_t)wi * c.ring * c.row_bytes;
+  uint64_t* bar = bars + wi * c.ring;
+  const uint64_t pol = policy_evict_first();
+  const size_t nstride = (size_t)c.BT * c.row_bytes;
+  const unsigned char* vb = reinterpret_cast<const unsigned char*>(v);
+
+  // The row stream is token-major: row q is source (q mod N) of the warp's
+  // token q / N. (iss_j, iss_n) is the next row to issue into the ring.
+  long long iss_j = 0;
+  int iss_n = 0;
+  long long issued = 0;
+  auto issue_next = [&](int slot_) {
+    if (lane == 0) {
+      const long long tok = tok0 + tstride * iss_j;
+      mbar_arrive_expect_tx(&bar[slot_], (uint32_t)c.row_bytes);
+      bulk_g2s(ring + (size_t)slot_ * c.row_bytes,
+               vb + (size_t)iss_n * nstride + (size_t)tok * c.row_bytes, (uint32_t)c.row_bytes,
+               &bar[slot_], pol);
+    }
+    ++issued;
+    if (++iss_n == c.N) {
+      iss_n = 0;
+      ++iss_j;
+    }
+  };
+  for (int s = 0; s < c.ring && issued < nrows; ++s) issue_next(s);
+
+  // Lane-chunk k of a row is chunk lane + 32k; past the row end (only when
+  // !FULL) it reads the zero pad instead.
+  auto cval = [&](int k) { return FULL || lane + 32 * k < c.row_chunks; };
+  const float inv_d = 1.f / (float)c.D;
+
+  int slot = 0;
+  uint32_t ph = 0;
+  for (long long j = 0; j < ntok; ++j) {
+    const long long tok = tok0 + tstride * j;
+    float* st = stats != nullptr ? stats + tok * c.stats_stride : nullptr;
+    float2 o[CPL][P];
+    float m = 0.f, l = 0.f;
+    for (int n = 0; n < c.N; ++n) {
+      if (!mbar_wait(&bar[slot], ph)) return;
+      const unsigned char* row = ring + (size_t)slot * c.row_bytes;
+      float2 x[CPL][P];
+#pragma unroll
+      for (int k = 0; k < CPL; ++k)
+        unpack2<T>(lds128(cval(k) ? row + (lane + 32 * k) * 16 : zero_pad), x[k]);
+      __syncwarp();
+      if (issued < nrows) {
+        if (lane == 0) fence_proxy_async();
+        issue_next(slot);
+      }
+      if (++slot == c.ring) {
+        slot = 0;
+        ph ^= 1u;
+      }
+
+      if constexpr (SOL) {
+#pragma unroll
+        for (int k = 0; k < CPL; ++k)
+#pragma unroll
+          for (int i = 0; i < P; ++i) o[k][i] = n == 0 ? x[k][i] : __fadd2_rn(o[k][i], x[k][i]);
+        continue;
+      } else {
+        // dot and sum of squares: two independent accumulator pairs each
+        float2 dacc[2], sacc[2];
+#pragma unroll
+        for (int a = 0; a < 2; ++a) dacc[a] = sacc[a] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < CPL; ++k) {
+          const float4* wp = reinterpret_cast<const float4*>(wsm) + (lane + 32 * k);
+#pragma unroll
+          for (int i = 0; i < P; i += 2) {
+            const float4 wv =
+                cval(k) ? wp[(i / 2) * c.row_chunks] : make_float4(0.f, 0.f, 0.f, 0.f);
+            dacc[0] = __ffma2_rn(make_float2(wv.x, wv.y), x[k][i], dacc[0]);
+            sacc[0] = __ffma2_rn(x[k][i], x[k][i], sacc[0]);
+            dacc[1] = __ffma2_rn(make_float2(wv.z, wv.w), x[k][i + 1], dacc[1]);
+            sacc[1] = __ffma2_rn(x[k][i + 1], x[k][i + 1], sacc[1]);
+          }
+        }
+        const float2 d2 = __fadd2_rn(dacc[0], dacc[1]);
+        const float2 s2 = __fadd2_rn(sacc[0], sacc[1]);
+        float dot = d2.x + d2.y, ssq = s2.x + s2.y;
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          dot += __shfl_xor_sync(kFull, dot, off);
+          ssq += __shfl_xor_sync(kFull, ssq, off);
+        }
+        const float r = rsqrtf(ssq * inv_d + c.eps);
+        const float logit = dot * r;
+        if (st != nullptr && lane == 0) {
+          st[n] = logit;
+          st[c.N + n] = r;
+        }
+        if (n == 0) {
+          m = logit;
+          l = 1.f;
+#pragma unroll
+          for (int k = 0; k < CPL; ++k)
+#pragma unroll
+            for (int i = 0; i < P; ++i) o[k][i] = x[k][i];
+        } else if (logit > m) {  // warp-uniform: logit is bitwise equal in all lanes
+          const float sc = expf(m - logit);
+          m = logit;
+          l = fmaf(l, sc, 1.f);
+#pragma unroll
+          for (int k = 0; k < CPL; ++k)
+#pragma unroll
+            for (int i = 0; i < P; ++i) o[k][i] = __ffma2_rn(o[k][i], f2(sc), x[k][i]);
+        } else {
+          const float p = expf(logit - m);
+          l += p;
+#pragma unroll
+          for (int k = 0; k < CPL; ++k)
+#pragma unroll
+            for (int i = 0; i < P; ++i) o[k][i] = __ffma2_rn(f2(p), x[k][i], o[k][i]);
+        }
+      }
+    }
+    if constexpr (!SOL) {
+      if (st != nullptr && lane == 0) {
+        st[2 * c.N] = m;
+        st[2 * c.N + 1] = m + logf(l);
+      }
+      const float inv = 1.f / l;
+#pragma unroll
+      for (int k = 0; k < CPL; ++k)
+#pragma unroll
+        for (int i = 0; i < P; ++i) o[k][i] = __fmul2_rn(o[k][i], f2(inv));
+    }
+    T* orow = out + tok * c.D;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k)
+      if (cval(k)) stg128(orow + (lane + 32 * k) * VEC, pack2<T>(o[k]));
+  }
+}
+
+cudaError_t launch_stream_fwd(const StreamCfg& c, int grid, int cpl, int dtype, const void* v,
+                              const void* w, int w_dtype, void* out, float* stats, bool sol,
+                              cudaStream_t st);
+
+template <typename T, bool SOL, bool FULL>
+cudaError_t launch_stream_tf(const StreamCfg& c, int grid, int cpl, const void* v, const void* w,
+                             int w_dtype, void* out, float* stats, cudaStream_t st) {
+  const size_t smem = stream_smem_layout(c).total;
+  const dim3 block(c.warps * 32);
+  const T* vp = static_cast<const T*>(v);
+  T* op = static_cast<T*>(out);
+  switch (cpl) {
+    case 1:
+      return launch_smem(stream_fwd_kernel<T, 1, SOL, FULL>, grid, block, smem, st, vp, w, w_dtype,
+                         op, stats, c);
+    case 2:
+      return launch_smem(stream_fwd_kernel<T, 2, SOL, FULL>, grid, block, smem, st, vp, w, w_dtype,
+                         op, stats, c);
+    case 4:
+      return launch_smem(stream_fwd_kernel<T, 4, SOL, FULL>, grid, block, smem, st, vp, w, w_dtype,
+                         op, stats, c);
+    case 8:
+      return launch_smem(stream_fwd_kernel<T, 8, SOL, FULL>, grid, block, smem, st, vp, w, w_dtype,
+                         op, stats, c);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+template <typename T, bool SOL>
+cudaError_t launch_stream_t(const StreamCfg& c, int grid, int cpl, const void* v, const void* w,
+                            int w_dtype, void* out, float* stats, cudaStream_t st) {
+  if (c.row_chunks == 32 * cpl)
+    return launch_stream_tf<T, SOL, true>(c, grid, cpl, v, w, w_dtype, out, stats, st);
+  return launch_stream_tf<T, SOL, false>(c, grid, cpl, v, w, w_dtype, out, stats, st);
+}
+
+}  // namespace sy

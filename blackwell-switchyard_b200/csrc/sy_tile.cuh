@@ -39,6 +39,7 @@ struct TileCfg {
   int stats_stride;  // floats per token in the statistics buffer
   int red_stride;    // floats per consumer warp in one reduction buffer
   int coef_stride;   // floats per consumer warp in the per-source coefficients
+  int w_smem;        // register-tile forward: w kept in shared memory (fp32)
   float eps;
 };
 
@@ -50,7 +51,7 @@ __host__ __device__ inline int tile_coef_stride(int N) { return 4 * ((N + 7) / 8
 
 // Shared-memory carve-up, identical on host (sizing) and device (pointers).
 struct TileSmem {
-  size_t stages_off, red_off, coef_off, bar_off, total;
+  size_t stages_off, red_off, coef_off, bar_off, zero_off, w_off, total;
 };
 
 __host__ __device__ inline TileSmem tile_smem_layout(const TileCfg& c) {
@@ -60,7 +61,9 @@ __host__ __device__ inline TileSmem tile_smem_layout(const TileCfg& c) {
   s.red_off = (size_t)c.stages * c.stage_bytes;
   s.coef_off = s.red_off + (size_t)2 * nwc * c.red_stride * sizeof(float);
   s.bar_off = s.coef_off + (size_t)nwc * c.coef_stride * sizeof(float);
-  s.total = s.bar_off + (size_t)2 * c.stages * sizeof(uint64_t);
+  s.zero_off = s.bar_off + (size_t)2 * c.stages * sizeof(uint64_t);  // 16 zero bytes
+  s.w_off = s.zero_off + 16;  // fp32 copy of w (w_smem != 0): D floats, 16-byte planes
+  s.total = s.w_off + (c.w_smem ? ((size_t)c.D * 4 + 15) / 16 * 16 : 0);
   return s;
 }
 

@@ -291,9 +291,9 @@ cudaError_t launch_tile_bwd(const TileCfg& c, int grid, int cpt, int dtype, cons
 
 // ---------------------------------------------------------------------------
 // dw[d] = sum_p part[p, d]. A CTA owns 32 consecutive columns; warp k of its 8
-// sums rows p = k, k+8, k+16, ... in increasing order, eight loads in flight
-// at a time (one fixed-order chain), then warp 0 adds the 8 warp sums in warp
-// order. Fixed order everywhere => deterministic.
+// sums rows p = k, k+8, k+16, ... in increasing order (loaded 32 at a time),
+// then warp 0 adds the 8 warp sums in warp order. Fixed order everywhere =>
+// deterministic.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict__ part, long long P,
                                                         long long D, void* __restrict__ dw,
@@ -305,15 +305,18 @@ __global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict_
   const long long col = (long long)blockIdx.x * 32 + lane;
   float acc = 0.f;
   if (col < D) {
-    long long p = wp;
-    for (; p + 56 < P; p += 64) {
-      float x[8];
+    // all of a batch's loads are issued before the first add: one DRAM
+    // round trip per 32 rows instead of one per row
+    for (long long p0 = wp; p0 < P; p0 += 8 * 32) {
+      float x[32];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) x[i] = __ldcs(part + (p + 8 * i) * D + col);
+      for (int i = 0; i < 32; ++i) {
+        const long long p = p0 + 8 * i;
+        x[i] = p < P ? __ldcs(part + p * D + col) : 0.f;
+      }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc += x[i];
+      for (int i = 0; i < 32; ++i) acc += x[i];
     }
-    for (; p < P; p += 8) acc += __ldcs(part + p * D + col);
   }
   slice[wp][lane] = acc;
   __syncthreads();

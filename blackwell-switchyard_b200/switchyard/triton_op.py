@@ -41,16 +41,17 @@ DEFAULT_EPS = 1e-6
 
 #: Kernel families reported by :func:`_plan` (``sy_plan_kind``): the generic
 #: any-shape kernels, the register-tile kernels (exact N <= 16) and the
-#: shared-memory tile kernels (run-time N <= 64), both TMA-pipelined.
-PLAN_GENERIC, PLAN_TILE, PLAN_SMEM_TILE = 0, 1, 2
+#: shared-memory tile kernels (run-time N <= 64), both TMA-pipelined, and the
+#: row-stream forward (one warp per token, online softmax over the sources).
+PLAN_GENERIC, PLAN_TILE, PLAN_SMEM_TILE, PLAN_STREAM = 0, 1, 2, 3
 
 
 def _plan(op: str, n: int, bt: int, d: int, dtype: torch.dtype, s: int = 1) -> int:
     """Which kernel family a shape dispatches to (the reference's
     ``_launch_config`` / ``_bwd_launch`` / ``_batched_launch`` counterpart).
 
-    ``op`` is ``"fwd"``, ``"bwd"`` or ``"batched"``. Returns :data:`PLAN_TILE`,
-    :data:`PLAN_SMEM_TILE` or :data:`PLAN_GENERIC`.
+    ``op`` is ``"fwd"``, ``"bwd"`` or ``"batched"``. Returns :data:`PLAN_STREAM`,
+    :data:`PLAN_TILE`, :data:`PLAN_SMEM_TILE` or :data:`PLAN_GENERIC`.
     """
     code = {"fwd": 0, "bwd": 1, "batched": 2}[op]
     k = _native.plan_kind(code, n, bt, d, s, dtype)
@@ -60,7 +61,8 @@ def _plan(op: str, n: int, bt: int, d: int, dtype: torch.dtype, s: int = 1) -> i
 
 
 def _strategy(n: int, bt: int, d: int, dtype: torch.dtype) -> str:
-    return {PLAN_GENERIC: "generic", PLAN_TILE: "register-tile", PLAN_SMEM_TILE: "smem-tile"}[
+    return {PLAN_GENERIC: "generic", PLAN_TILE: "register-tile", PLAN_SMEM_TILE: "smem-tile",
+            PLAN_STREAM: "row-stream"}[
         _plan("fwd", n, bt, d, dtype)
     ]
 

@@ -131,7 +131,8 @@ SY_API int sy_speed_of_light(const void* v, void* out, int64_t N, int64_t BT,
  * Which kernel family sy_fwd / sy_bwd / sy_fwd_batched would launch for a
  * shape on the current device, without launching: 1 = register-tile kernel
  * (exact N, TMA-pipelined), 2 = shared-memory tile kernel (run-time N,
- * TMA-pipelined), 0 = generic (any size/alignment) kernel, <0 = -status.
+ * TMA-pipelined), 3 = row-stream kernel (one warp per token, online softmax,
+ * forward only), 0 = generic (any size/alignment) kernel, <0 = -status.
  * `op` is 0 forward, 1 backward, 2 batched (S queries), 3 speed of light.
  * Used by tests to pin dispatch, like the reference's _launch_config tests
  * (src/switchyard/triton_op.py:130-150, :267-276, :420-435).
@@ -144,8 +145,10 @@ SY_API int sy_plan_kind(int op, int64_t N, int64_t BT, int64_t D, int64_t S,
  * and `max_smem` bytes of opt-in shared memory per block (pass 0, 0 for the
  * current device). Writes out[8] = {kind (as sy_plan_kind), grid, pipeline
  * stages, consumer groups, threads per group, 16-byte chunks per thread per
- * row, bytes per stage, dynamic shared memory bytes}. No reference
- * counterpart; exposes the planner to tests.
+ * row, bytes per stage, dynamic shared memory bytes}; for the row-stream
+ * kind: {3, grid, row buffers per warp, warps per CTA, 32, chunks per lane,
+ * bytes per row, shared memory bytes}. No reference counterpart; exposes the
+ * planner to tests.
  */
 SY_API int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S,
                         int dtype, int sms, int max_smem, int64_t* out);

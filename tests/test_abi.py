@@ -105,17 +105,28 @@ def test_planner_invariants_for_b200(native, dtype_name):
                     continue
                 assert p["smem_bytes"] <= B200["max_smem"]
                 assert p["stages"] >= 2 and p["groups"] >= 1
-                assert p["groups"] * p["threads_per_group"] <= 256
-                assert p["threads_per_group"] % 32 == 0
                 assert p["grid"] == 148
-                assert p["chunks_per_thread"] * p["threads_per_group"] * 16 >= d * dt.itemsize
+                if p["kind"] == 3:
+                    continue_checks = False
+                else:
+                    continue_checks = True
+                if continue_checks:
+                    # register-tile CTAs have up to 512 threads, shared-memory tile ones 256
+                    assert p["groups"] * p["threads_per_group"] <= (512 if p["kind"] == 1 else 256)
+                    assert p["threads_per_group"] % 32 == 0
+                    assert p["chunks_per_thread"] * p["threads_per_group"] * 16 >= d * dt.itemsize
                 if p["kind"] == 2:
                     assert p["stages"] % p["groups"] == 0
                     assert n <= 64
                 if p["kind"] == 1:
                     assert n <= 16
+                if p["kind"] == 3:  # row stream: forward only, 32 lanes x chunks >= row
+                    assert op == 0 and p["threads_per_group"] == 32
+                    assert p["chunks_per_thread"] * 32 * 16 >= d * dt.itemsize
+                    assert p["groups"] * 32 <= 512 and p["stages"] >= 2
     rep = native.plan_info(0, 9, 4096, 2048, 1, torch.bfloat16, **B200)
-    assert rep["kind"] == 1 and rep["stages"] >= 4
+    assert rep["kind"] == 1 and rep["stages"] >= 4  # register tile, >= 4 tokens in flight
+    assert native.plan_info(0, 17, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 3
     assert native.plan_info(1, 9, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 1
     # rows that are not a multiple of 16 bytes go to the generic kernels
     assert native.plan_info(0, 3, 64, 777, 1, torch.bfloat16, **B200)["kind"] == 0

@@ -23,7 +23,7 @@ from switchyard import (  # noqa: E402
     speed_of_light,
 )
 from switchyard import _native  # noqa: E402
-from switchyard.triton_op import DEFAULT_EPS, PLAN_GENERIC, PLAN_TILE, _plan  # noqa: E402
+from switchyard.triton_op import DEFAULT_EPS, PLAN_GENERIC, PLAN_STREAM, PLAN_TILE, _plan  # noqa: E402
 
 DEV = "cuda"
 
@@ -153,6 +153,8 @@ def test_dispatch_sends_the_representative_shape_to_the_tile_kernels():
     for n in range(1, 10):  # every source count the 24-layer 8-block model uses
         assert _plan("fwd", n, 8192, 2048, torch.bfloat16) == PLAN_TILE
         assert _plan("bwd", n, 8192, 2048, torch.bfloat16) == PLAN_TILE
+    # more sources than the register tile holds: the row-stream forward
+    assert _plan("fwd", 17, 4096, 2048, torch.bfloat16) == PLAN_STREAM
     # rows that are not a multiple of 16 bytes take the generic kernels
     assert _plan("fwd", 3, 64, 777, torch.bfloat16) == PLAN_GENERIC
     assert _plan("bwd", 5, 17, 63, torch.float32) == PLAN_GENERIC
