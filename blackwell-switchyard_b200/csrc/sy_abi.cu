@@ -116,7 +116,10 @@ bool size_ring(TileCfg& c, int op, int groups, const DevInfo& di, int64_t* smem_
   // at least two stages, so one can load while it computes on the other.
   // (The register-tile kernels give every group its own ring instead, which
   // has no such constraint.)
-  while (groups > 1 && stages < 2 * groups) --groups;
+  // With per-group rings (the register-tile kernels refill a stage as soon as
+  // the group holds it in registers) one stage per group already overlaps
+  // loads with compute.
+  while (groups > 1 && stages < (per_group_rings ? 1 : 2) * groups) --groups;
   if (!per_group_rings) stages = stages / groups * groups;
   c.groups = groups;
   c.stages = (int)stages;
@@ -155,7 +158,15 @@ TilePlan plan_tile(int op, int64_t N, int64_t BT, int64_t D, int dtype, const De
     // is then kept packed), backward: up to 2 (N <= 9, more live state).
     // Never so many that a warp's lanes would sit idle.
     int cpt = 0, tg = 0;
-    const int max_cpt = N <= kRegMaxN4 && op == kOpFwd ? 4 : (N <= kRegMaxN2 ? 2 : 1);
+    // The stage-held forward keeps no tile in registers: four chunks for any
+    // N <= 9, in groups of (at D=2048 bf16) two warps, kHoldThreads per CTA.
+    // With one stage per group its groups start in lockstep (all load, then
+    // all compute), which only evens out over many tokens per SM; below
+    // kHoldMinTokensPerSM the register tile (stage refilled as soon as the
+    // tile is in registers) is faster.
+    const bool hold = op == kOpFwd && SY_TUNE_FWD_HOLD && N <= kRegFwdMaxN &&
+                      BT >= (int64_t)kHoldMinTokensPerSM * di.sms;
+    const int max_cpt = hold ? 4 : (N <= kRegMaxN4 && op == kOpFwd ? 4 : (N <= kRegMaxN2 ? 2 : 1));
     for (int cand = max_cpt; cand >= 1 && !cpt; cand /= 2) {
       if (cand > 1 && rc < 32 * cand) continue;  // lanes would be idle
       const int64_t t = round32((rc + cand - 1) / cand);
@@ -166,7 +177,8 @@ TilePlan plan_tile(int op, int64_t N, int64_t BT, int64_t D, int dtype, const De
       rcfg.tg = tg;
       rcfg.coef_stride = op == kOpBwd ? tile_coef_stride((int)N) : 0;  // bwd: float4 per source
       rcfg.w_smem = op == kOpBwd ? 0 : 1;  // forward reads its fp32 w from shared memory
-      int groups = reg_threads((int)N, cpt, op == kOpBwd) / tg;
+      rcfg.hold = hold ? 1 : 0;
+      int groups = (hold ? kHoldThreads : reg_threads((int)N, cpt, 16 / es, op == kOpBwd)) / tg;
       if (groups > 16) groups = 16;  // named barrier ids 1..15 (1-warp groups use none)
       if (SY_TUNE_GROUPS > 0) groups = SY_TUNE_GROUPS;
       if (size_ring(rcfg, op, groups < 1 ? 1 : groups, di, &p.smem, /*per_group_rings=*/true)) {

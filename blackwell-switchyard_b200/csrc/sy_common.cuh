@@ -138,6 +138,15 @@ __device__ __forceinline__ uint4 lds128(const void* p) {
   return *reinterpret_cast<const uint4*>(p);
 }
 
+// A shared-memory float4 load the compiler may not merge with another.
+__device__ __forceinline__ float4 lds128_f4_volatile(const void* p) {
+  float4 v;
+  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(static_cast<uint32_t>(__cvta_generic_to_shared(p))));
+  return v;
+}
+
 __device__ __forceinline__ void stg128(void* p, const uint4& v) {
   // Output is written once and not re-read by this kernel: stream it.
   __stcs(reinterpret_cast<uint4*>(p), v);

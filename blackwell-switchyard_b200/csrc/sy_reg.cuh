@@ -36,19 +36,30 @@ constexpr int kRegMaxN = 16;
 constexpr int kRegMaxN2 = 9;   // two chunks per thread up to this N
 constexpr int kRegMaxN4 = 6;   // forward: four chunks per thread up to this N
 constexpr int kRegFwdMaxN = 9; // forward: larger N takes the row-stream kernel
+constexpr int kHoldThreads = 384;        // CTA size of the stage-held forward
+constexpr int kHoldMinTokensPerSM = 64;  // use it from this many tokens per SM
 
-#ifndef SY_TUNE_REG_FWD_THREADS
-#define SY_TUNE_REG_FWD_THREADS 256
+#ifndef SY_TUNE_FWD_HOLD
+#define SY_TUNE_FWD_HOLD 1  // forward N <= 9: stage-held tile (1) or register tile (0)
 #endif
-#ifndef SY_TUNE_REG_BWD_THREADS
-#define SY_TUNE_REG_BWD_THREADS 256
+
+#ifndef SY_TUNE_FWD_UNPACKED_MAX
+#define SY_TUNE_FWD_UNPACKED_MAX 144  // largest forward tile kept as fp32 (floats)
 #endif
+#ifndef SY_TUNE_FWD_PACKED_THREADS
+#define SY_TUNE_FWD_PACKED_THREADS 256
+#endif
+
+// Forward tile storage: fp32 (unpacked once) when it is small, else the raw
+// 16-byte words, unpacked at each use.
+__host__ __device__ constexpr bool reg_fwd_packed(int n, int cpt, int vec) {
+  return n * cpt * vec > SY_TUNE_FWD_UNPACKED_MAX;
+}
 
 // Threads per CTA of a register-tile instantiation (the launch bound that sets
-// the register budget): 256, i.e. up to 255 registers per thread -- room for
-// the forward's unpacked fp32 tile (N * CPT * VEC floats, 144 at N=9 bf16).
-__host__ __device__ constexpr int reg_threads(int /*n*/, int /*cpt*/, bool bwd) {
-  return bwd ? SY_TUNE_REG_BWD_THREADS : SY_TUNE_REG_FWD_THREADS;
+// the register budget): 256, i.e. up to 255 registers per thread.
+__host__ __device__ constexpr int reg_threads(int n, int cpt, int vec, bool bwd) {
+  return (!bwd && reg_fwd_packed(n, cpt, vec)) ? SY_TUNE_FWD_PACKED_THREADS : 256;
 }
 
 // A token's register tile: N rows x CPT chunks, held either as fp32 pairs
@@ -175,8 +186,11 @@ __device__ __forceinline__ void issue_token(unsigned char* dst, uint64_t* bar, c
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
-template <typename T, int N, int CPT>
-__global__ void __launch_bounds__(reg_threads(N, CPT, false), 1)
+// HOLD: the tile is not copied to registers; both phases read it from the
+// stage, which is refilled only after the group's second barrier (after
+// phase B). Far fewer registers per thread, so more groups per CTA.
+template <typename T, int N, int CPT, bool HOLD>
+__global__ void __launch_bounds__(HOLD ? kHoldThreads : reg_threads(N, CPT, Dt<T>::kVec, false), 1)
     reg_fwd_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
                    T* __restrict__ out, float* __restrict__ stats, const TileCfg c) {
   constexpr int VEC = Dt<T>::kVec;
@@ -255,46 +269,78 @@ __global__ void __launch_bounds__(reg_threads(N, CPT, false), 1)
       cs[cc] = cv[cc] ? c.row_bytes : 0;
     }
     // The tile stays packed (16-byte words) when unpacking it would not fit
-    // the register budget; it is then unpacked again in phase B.
-    constexpr bool PACKED = N * CPT * VEC > 144;
-    Tile<T, N, CPT, PACKED> x;
+    // the register budget; it is then unpacked again in phase B. In HOLD
+    // mode it stays in the stage and is read from there in both phases.
+    constexpr bool PACKED = reg_fwd_packed(N, CPT, VEC);
+    Tile<T, HOLD ? 1 : N, HOLD ? 1 : CPT, PACKED> x;
+    if constexpr (!HOLD) {
 #pragma unroll
-    for (int n = 0; n < N; ++n)
+      for (int n = 0; n < N; ++n)
 #pragma unroll
-      for (int cc = 0; cc < CPT; ++cc) x.load(n, cc, lds128(cb[cc] + n * cs[cc]));
-    // chunk-outer: the chunk's w (fp32, from shared memory) is read once and
-    // every row accumulates into its own dot / sum-of-squares pair
-    float2 dot2[N], ssq2[N];
-#pragma unroll
-    for (int n = 0; n < N; ++n) dot2[n] = ssq2[n] = make_float2(0.f, 0.f);
-#pragma unroll
-    for (int cc = 0; cc < CPT; ++cc) {
-      float2 wv[P];
-      const float4* wp = reinterpret_cast<const float4*>(wsm) + (tig + cc * c.tg);
-#pragma unroll
-      for (int i = 0; i < P; i += 2) {
-        const float4 q = cv[cc] ? wp[(i / 2) * c.row_chunks] : make_float4(0.f, 0.f, 0.f, 0.f);
-        wv[i] = make_float2(q.x, q.y);
-        wv[i + 1] = make_float2(q.z, q.w);
-      }
-#pragma unroll
-      for (int n = 0; n < N; ++n) {
-        float2 p[P];
-        x.get(n, cc, p);
-#pragma unroll
-        for (int i = 0; i < P; ++i) {
-          dot2[n] = __ffma2_rn(wv[i], p[i], dot2[n]);
-          ssq2[n] = __ffma2_rn(p[i], p[i], ssq2[n]);
-        }
-      }
+        for (int cc = 0; cc < CPT; ++cc) x.load(n, cc, lds128(cb[cc] + n * cs[cc]));
     }
+    auto tget = [&](int n, int cc, float2* p) {
+      if constexpr (HOLD)
+        unpack2<T>(lds128(cb[cc] + n * cs[cc]), p);
+      else
+        x.get(n, cc, p);
+    };
+    // w (fp32, shared memory) for chunk cc, pair i. The load is volatile so
+    // the compiler re-reads w per row instead of keeping it in registers,
+    // which is the point of the row-outer loop below.
+    auto wpair = [&](int cc, int i) {
+      const float4* wp = reinterpret_cast<const float4*>(wsm) + (tig + cc * c.tg);
+      float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (cv[cc]) q = lds128_f4_volatile(wp + (i / 2) * c.row_chunks);
+      return (i & 1) ? make_float2(q.z, q.w) : make_float2(q.x, q.y);
+    };
     float a[M];
 #pragma unroll
     for (int i = 0; i < M; ++i) a[i] = 0.f;
+    if constexpr (PACKED && !HOLD) {
+      // row-outer, w re-read per row: two accumulators live instead of 2N
 #pragma unroll
-    for (int n = 0; n < N; ++n) {
-      a[n] = dot2[n].x + dot2[n].y;
-      a[HALF + n] = ssq2[n].x + ssq2[n].y;
+      for (int n = 0; n < N; ++n) {
+        float2 dot = make_float2(0.f, 0.f), ssq = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int cc = 0; cc < CPT; ++cc) {
+          float2 p[P];
+          tget(n, cc, p);
+#pragma unroll
+          for (int i = 0; i < P; ++i) {
+            dot = __ffma2_rn(wpair(cc, i), p[i], dot);
+            ssq = __ffma2_rn(p[i], p[i], ssq);
+          }
+        }
+        a[n] = dot.x + dot.y;
+        a[HALF + n] = ssq.x + ssq.y;
+      }
+    } else {
+      // chunk-outer: the chunk's w is read once, every row keeps its pairs
+      float2 dot2[N], ssq2[N];
+#pragma unroll
+      for (int n = 0; n < N; ++n) dot2[n] = ssq2[n] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int cc = 0; cc < CPT; ++cc) {
+        float2 wv[P];
+#pragma unroll
+        for (int i = 0; i < P; ++i) wv[i] = wpair(cc, i);
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+          float2 p[P];
+          tget(n, cc, p);
+#pragma unroll
+          for (int i = 0; i < P; ++i) {
+            dot2[n] = __ffma2_rn(wv[i], p[i], dot2[n]);
+            ssq2[n] = __ffma2_rn(p[i], p[i], ssq2[n]);
+          }
+        }
+      }
+#pragma unroll
+      for (int n = 0; n < N; ++n) {
+        a[n] = dot2[n].x + dot2[n].y;
+        a[HALF + n] = ssq2[n].x + ssq2[n].y;
+      }
     }
     // ---- cross-thread reduction ----
     const float tot_l = warp_reduce_scatter<M>(a, lane);
@@ -305,8 +351,8 @@ __global__ void __launch_bounds__(reg_threads(N, CPT, false), 1)
     else
       __syncwarp();
     // The whole group now holds the stage in registers: refill it with the
-    // group's token ring.cnt ahead.
-    if (tig == 0 && j + ring.cnt < ntok_g) {
+    // group's token ring.cnt ahead. (HOLD: after phase B instead.)
+    if (!HOLD && tig == 0 && j + ring.cnt < ntok_g) {
       fence_proxy_async();
       issue_token(stage0 + (size_t)sidx * c.stage_bytes, &full[sidx], vb,
                   cta + (long long)(g + (j + ring.cnt) * c.groups) * grid, N, c.row_bytes, nstride,
@@ -351,11 +397,24 @@ __global__ void __launch_bounds__(reg_threads(N, CPT, false), 1)
 #pragma unroll
       for (int n = 0; n < N; ++n) {
         float2 p[P];
-        x.get(n, cc, p);
+        tget(n, cc, p);
 #pragma unroll
         for (int i = 0; i < P; ++i) o[i] = __ffma2_rn(f2(al[n]), p[i], o[i]);
       }
       stg128(orow + (tig + cc * c.tg) * VEC, pack2<T>(o));
+    }
+    if constexpr (HOLD) {
+      // every warp of the group is done with the stage: refill it
+      if (wpg > 1)
+        named_sync(1 + g, c.tg);
+      else
+        __syncwarp();
+      if (tig == 0 && j + ring.cnt < ntok_g) {
+        fence_proxy_async();
+        issue_token(stage0 + (size_t)sidx * c.stage_bytes, &full[sidx], vb,
+                    cta + (long long)(g + (j + ring.cnt) * c.groups) * grid, N, c.row_bytes,
+                    nstride, nullptr, nullptr, 0, pol);
+      }
     }
 
     if (++slot == ring.cnt) {
@@ -370,7 +429,7 @@ __global__ void __launch_bounds__(reg_threads(N, CPT, false), 1)
 // backward (see sy_tile_bwd.cu for the formulas)
 // ---------------------------------------------------------------------------
 template <typename T, int N, int CPT>
-__global__ void __launch_bounds__(reg_threads(N, CPT, true), 1)
+__global__ void __launch_bounds__(reg_threads(N, CPT, Dt<T>::kVec, true), 1)
     reg_bwd_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
                    const T* __restrict__ gin, const float* __restrict__ stats, T* __restrict__ dv,
                    float* __restrict__ dw_partial, const TileCfg c) {
@@ -580,16 +639,33 @@ cudaError_t launch_reg_fwd_n(const TileCfg& c, int grid, int cpt, const void* v,
   const dim3 block(c.groups * c.tg);  // no producer warp
   const T* vp = static_cast<const T*>(v);
   T* op = static_cast<T*>(out);
+  if (c.hold) {
+    if ((int)block.x > kHoldThreads) return cudaErrorInvalidConfiguration;
+    if constexpr (N <= kRegFwdMaxN) {
+      if (cpt == 4)
+        return launch_smem(reg_fwd_kernel<T, N, 4, true>, grid, block, smem, st, vp, w, w_dtype,
+                           op, stats, c);
+      if (cpt == 2)
+        return launch_smem(reg_fwd_kernel<T, N, 2, true>, grid, block, smem, st, vp, w, w_dtype,
+                           op, stats, c);
+      if (cpt == 1)
+        return launch_smem(reg_fwd_kernel<T, N, 1, true>, grid, block, smem, st, vp, w, w_dtype,
+                           op, stats, c);
+    }
+    return cudaErrorInvalidValue;
+  }
+  if ((int)block.x > reg_threads(N, cpt, Dt<T>::kVec, false)) return cudaErrorInvalidConfiguration;
   if (cpt == 1)
-    return launch_smem(reg_fwd_kernel<T, N, 1>, grid, block, smem, st, vp, w, w_dtype, op, stats, c);
+    return launch_smem(reg_fwd_kernel<T, N, 1, false>, grid, block, smem, st, vp, w, w_dtype, op,
+                       stats, c);
   if constexpr (N <= kRegMaxN2)
     if (cpt == 2)
-      return launch_smem(reg_fwd_kernel<T, N, 2>, grid, block, smem, st, vp, w, w_dtype, op, stats,
-                         c);
+      return launch_smem(reg_fwd_kernel<T, N, 2, false>, grid, block, smem, st, vp, w, w_dtype, op,
+                         stats, c);
   if constexpr (N <= kRegMaxN4)
     if (cpt == 4)
-      return launch_smem(reg_fwd_kernel<T, N, 4>, grid, block, smem, st, vp, w, w_dtype, op, stats,
-                         c);
+      return launch_smem(reg_fwd_kernel<T, N, 4, false>, grid, block, smem, st, vp, w, w_dtype, op,
+                         stats, c);
   return cudaErrorInvalidValue;
 }
 
@@ -599,6 +675,7 @@ cudaError_t launch_reg_bwd_n(const TileCfg& c, int grid, int cpt, const void* v,
                              cudaStream_t st) {
   const size_t smem = tile_smem_layout(c).total;
   const dim3 block(c.groups * c.tg);  // no producer warp
+  if ((int)block.x > reg_threads(N, cpt, Dt<T>::kVec, true)) return cudaErrorInvalidConfiguration;
   const T* vp = static_cast<const T*>(v);
   const T* gp = static_cast<const T*>(g);
   T* dvp = static_cast<T*>(dv);

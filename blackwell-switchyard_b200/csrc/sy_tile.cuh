@@ -40,6 +40,7 @@ struct TileCfg {
   int red_stride;    // floats per consumer warp in one reduction buffer
   int coef_stride;   // floats per consumer warp in the per-source coefficients
   int w_smem;        // register-tile forward: w kept in shared memory (fp32)
+  int hold;          // register-tile forward: tile held in the stage (no register copy)
   float eps;
 };
 
