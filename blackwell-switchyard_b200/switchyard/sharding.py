@@ -37,8 +37,9 @@ def exchange_dw(dw_local: torch.Tensor, group=None) -> torch.Tensor:
     if dw_local.dtype != torch.float32 or dw_local.ndim != 1:
         raise ValueError("dw partial must be a 1-D float32 tensor")
     world = dist.get_world_size(group)
-    gathered = torch.empty(world, dw_local.numel(), dtype=torch.float32, device=dw_local.device)
-    dist.all_gather_into_tensor(gathered, dw_local.contiguous(), group=group)
+    flat = torch.empty(world * dw_local.numel(), dtype=torch.float32, device=dw_local.device)
+    dist.all_gather_into_tensor(flat, dw_local.contiguous(), group=group)
+    gathered = flat.view(world, dw_local.numel())
     total = gathered[0].clone()
     for r in range(1, world):
         total += gathered[r]
