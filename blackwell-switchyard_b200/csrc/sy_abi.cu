@@ -341,6 +341,9 @@ const char* sy_status_string(int status) {
       return t_last_error[0] ? t_last_error : "CUDA error";
     case SY_ERR_DEVICE:
       return "a kernel recorded a device-side error (bounded wait expired)";
+    case SY_ERR_SCRATCH:
+      return "shape needs more dw scratch than sy_bwd_noalloc's fixed array holds "
+             "(partial rows x D > sy_bwd_noalloc_max_floats()); use sy_bwd with a caller buffer";
     default:
       return "unknown status";
   }

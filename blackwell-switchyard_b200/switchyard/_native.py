@@ -21,6 +21,7 @@ LIB_PATH = Path(os.environ.get("SWITCHYARD_B200_LIB", Path(__file__).resolve().p
 
 SY_BF16, SY_F16, SY_F32 = 0, 1, 2
 SY_OK, SY_ERR_ARG, SY_ERR_DTYPE, SY_ERR_UNSUPPORTED, SY_ERR_CUDA, SY_ERR_DEVICE = range(6)
+SY_ERR_SCRATCH = 6
 
 DTYPE_CODES = {torch.bfloat16: SY_BF16, torch.float16: SY_F16, torch.float32: SY_F32}
 
@@ -40,6 +41,8 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sy_plan_kind": ([_I, _I64, _I64, _I64, _I64, _I], _I),
     "sy_plan_info": ([_I, _I64, _I64, _I64, _I64, _I, _I, _I, _c.POINTER(_I64)], _I),
     "sy_device_error": ([_c.POINTER(_c.c_int)], _I),
+    "sy_bwd_noalloc": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _F, _P], _I),
+    "sy_bwd_noalloc_max_floats": ([], _I64),
 }
 
 

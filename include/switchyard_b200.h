@@ -54,6 +54,8 @@ extern "C" {
 #define SY_ERR_UNSUPPORTED 3 /* shape outside every kernel's limits          */
 #define SY_ERR_CUDA 4        /* a CUDA runtime call or launch failed         */
 #define SY_ERR_DEVICE 5      /* a kernel reported a device-side error word   */
+#define SY_ERR_SCRATCH 6     /* shape needs more than sy_bwd_noalloc's fixed
+                                scratch (sy_bwd_noalloc_max_floats floats)  */
 
 typedef void* sy_stream_t; /* a cudaStream_t */
 
@@ -152,6 +154,26 @@ SY_API int sy_plan_kind(int op, int64_t N, int64_t BT, int64_t D, int64_t S,
  */
 SY_API int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S,
                         int dtype, int sms, int max_smem, int64_t* out);
+
+/*
+ * Backward plus dw reduction for callers that cannot allocate device memory
+ * (a plugin in a host framework that owns all device memory, or a
+ * latency-critical loop that must not allocate). Same arguments and results as
+ * sy_bwd followed by sy_dw_reduce, but the fp32 dw partial rows live in a
+ * fixed 8 MiB array inside the library instead of a caller buffer: shapes with
+ * sy_bwd_partials(N, BT, D, dtype) * D > sy_bwd_noalloc_max_floats() fail with
+ * SY_ERR_SCRATCH. The first call on a device looks the array up (make it before
+ * any stream capture); all calls on a device share the array, so calls that
+ * overlap on the GPU race. Allocates nothing. No counterpart in the reference.
+ */
+SY_API int sy_bwd_noalloc(const void* v, const void* w, const void* g,
+                          const float* stats, void* dv, void* dw, int64_t N,
+                          int64_t BT, int64_t D, int dtype, int w_dtype,
+                          float eps, sy_stream_t stream);
+
+/* Capacity of sy_bwd_noalloc's scratch array, in fp32 values. No counterpart
+ * in the reference. */
+SY_API int64_t sy_bwd_noalloc_max_floats(void);
 
 /*
  * Reads the device-side error word of the current device and clears it.

@@ -51,7 +51,7 @@ def test_library_is_built_for_sm100a_only():
 
 
 def test_status_strings(native):
-    for code in range(6):
+    for code in range(7):
         assert native.lib.sy_status_string(code)
     assert native.lib.sy_version().startswith(b"switchyard-b200")
 
