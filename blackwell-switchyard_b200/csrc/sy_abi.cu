@@ -25,6 +25,9 @@
 #ifndef SY_TUNE_PDL
 #define SY_TUNE_PDL 1  // launch the dw reduction as a programmatic dependent
 #endif
+#ifndef SY_TUNE_STREAM_REREAD
+#define SY_TUNE_STREAM_REREAD 1  // forward, 8 chunks per lane: re-read row stream first
+#endif
 
 namespace sy {
 
@@ -227,7 +230,8 @@ struct StreamPlan {
 // Row-stream forward (one warp per token, online softmax): rows must be a
 // multiple of 16 bytes and fit 8 16-byte chunks per lane (bf16/f16 D <= 2048,
 // fp32 D <= 1024); any N.
-StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInfo& di) {
+StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInfo& di,
+                       bool sol = false) {
   StreamPlan p;
   const int es = esize_of(dtype);
   if (!es || N < 1 || D < 1 || D > kMaxD || BT < 1 || BT > INT_MAX) return p;
@@ -242,7 +246,19 @@ StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInf
   c.D = (int)D;
   c.row_chunks = (int)rc;
   c.row_bytes = (int)(D * es);
-  c.warps = stream_threads(cpl) / 32;
+  c.reread = (SY_TUNE_STREAM_REREAD && cpl == 8 && !sol) ? 1 : 0;
+  c.warps = stream_threads(cpl, c.reread != 0) / 32;
+  if (c.reread) {
+    // Whole tokens per warp, as even as possible: with t tokens per CTA and
+    // at most M warps, k = ceil(t / M) tokens per warp and ceil(t / k) warps,
+    // so no warp has more tokens than necessary (4096 tokens on 148 SMs:
+    // 14 warps x 2).
+    const int64_t g0 = BT < di.sms ? BT : di.sms;
+    const int64_t t = (BT + g0 - 1) / g0;
+    const int64_t mw = kStreamRereadThreads / 32;
+    const int64_t k = (t + mw - 1) / mw;
+    c.warps = (int)((t + k - 1) / k);
+  }
   c.stats_stride = (int)stats_stride(N);
   c.ring = 0;
   const int64_t fixed = (int64_t)stream_smem_layout(c).total;
@@ -254,6 +270,7 @@ StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInf
   if (p.smem > di.max_smem) return p;
   const int64_t need = (BT + c.warps - 1) / c.warps;  // CTAs with work for every warp
   p.grid = (int)(need < di.sms ? need : di.sms);
+  if (c.reread) p.grid = (int)(BT < di.sms ? BT : di.sms);
   p.c = c;
   p.cpl = cpl;
   p.ok = true;
@@ -365,12 +382,21 @@ int sy_fwd(const void* v, const void* w, void* out, float* stats, int64_t N, int
   if (e != cudaSuccess) return cuda_status(e, "sy_fwd: device query");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool aligned = al16(v) && al16(out);
-  const TilePlan p = plan_tile(kOpFwd, N, BT, D, dtype, di);
+  // The planners size kernels from the shape alone; eps is set here. Order:
+  // the re-read row stream (4 KiB rows, any N), the register tile (N <= 9),
+  // the row stream (rows up to 4 KiB), the shared-memory tile, generic.
+  StreamPlan sp = plan_stream(N, BT, D, dtype, di);
+  sp.c.eps = eps;
+  if (sp.ok && sp.c.reread && aligned) {
+    e = launch_stream_fwd(sp.c, sp.grid, sp.cpl, dtype, v, w, w_dtype, out, stats, false, st);
+    return cuda_status(e, "sy_fwd: stream kernel launch");
+  }
+  TilePlan p = plan_tile(kOpFwd, N, BT, D, dtype, di);
+  p.c.eps = eps;
   if (p.kind == kPlanRegTile && aligned) {
     e = launch_plan_fwd(p, dtype, v, w, w_dtype, out, stats, st);
     return cuda_status(e, "sy_fwd: register-tile kernel launch");
   }
-  const StreamPlan sp = plan_stream(N, BT, D, dtype, di);
   if (sp.ok && aligned) {
     e = launch_stream_fwd(sp.c, sp.grid, sp.cpl, dtype, v, w, w_dtype, out, stats, false, st);
     return cuda_status(e, "sy_fwd: stream kernel launch");
@@ -415,7 +441,8 @@ int sy_bwd(const void* v, const void* w, const void* g, const float* stats, void
   DevInfo di;
   cudaError_t e = dev_info(&di);
   if (e != cudaSuccess) return cuda_status(e, "sy_bwd: device query");
-  const TilePlan p = plan_tile(kOpBwd, N, BT, D, dtype, di);
+  TilePlan p = plan_tile(kOpBwd, N, BT, D, dtype, di);
+  p.c.eps = eps;
   if (p.kind != kPlanGeneric && al16(v) && al16(g) && al16(stats) && al16(dv) &&
       al16(dw_partial)) {
     e = launch_plan_bwd(p, dtype, v, w, w_dtype, g, stats, dv, dw_partial, st);
@@ -468,7 +495,7 @@ int sy_speed_of_light(const void* v, void* out, int64_t N, int64_t BT, int64_t D
   cudaError_t e = dev_info(&di);
   if (e != cudaSuccess) return cuda_status(e, "sy_speed_of_light: device query");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const StreamPlan sp = plan_stream(N, BT, D, dtype, di);
+  const StreamPlan sp = plan_stream(N, BT, D, dtype, di, /*sol=*/true);
   if (sp.ok && al16(v) && al16(out)) {
     e = launch_stream_fwd(sp.c, sp.grid, sp.cpl, dtype, v, nullptr, SY_F32, out, nullptr, true, st);
     return cuda_status(e, "sy_speed_of_light: stream kernel launch");
@@ -499,9 +526,9 @@ int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype,
   int top = op == 1 ? kOpBwd : (op == 3 ? kOpSol : kOpFwd);
   if (op == 2 && S < 1) return SY_ERR_ARG;
   if (top != kOpBwd && (op != 2 || S == 1)) {
-    const StreamPlan sp = plan_stream(N, bt, D, dtype, di);
-    const bool reg_first =
-        top == kOpFwd && plan_tile(kOpFwd, N, bt, D, dtype, di).kind == kPlanRegTile;
+    const StreamPlan sp = plan_stream(N, bt, D, dtype, di, top == kOpSol);
+    const bool reg_first = top == kOpFwd && !sp.c.reread &&
+                           plan_tile(kOpFwd, N, bt, D, dtype, di).kind == kPlanRegTile;
     if (sp.ok && !reg_first) {
       out[0] = kPlanStream;
       out[1] = sp.grid;

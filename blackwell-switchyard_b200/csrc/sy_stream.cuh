@@ -39,6 +39,7 @@ struct StreamCfg {
   int warps;         // W per CTA
   int ring;          // R row buffers per warp
   int stats_stride;
+  int reread;        // 1: second pass reads the row again from shared memory
   float eps;
 };
 
@@ -63,12 +64,21 @@ __host__ __device__ inline StreamSmem stream_smem_layout(const StreamCfg& c) {
 // Threads per CTA for CPL chunks per lane. The fp32 row and the fp32 output
 // accumulator take 2 * 4 * CPL registers per lane (64 each at CPL=8 bf16),
 // so CPL <= 4 runs 16 warps per SM and CPL = 8 twelve (168 registers each).
-__host__ __device__ constexpr int stream_threads(int cpl) {
-  return cpl <= 4 ? 512 : SY_TUNE_STREAM8_THREADS;
+// REREAD drops the fp32 row from the registers (the second pass reads it from
+// shared memory again), which leaves room for 14 warps at CPL = 8.
+#ifndef SY_TUNE_REREAD_WARPS
+#define SY_TUNE_REREAD_WARPS 14
+#endif
+// Up to 14 warps. (The register file is split between the SM's four warp
+// schedulers, so anything over 12 warps caps a thread at 128 registers.)
+constexpr int kStreamRereadThreads = 32 * SY_TUNE_REREAD_WARPS;
+__host__ __device__ constexpr int stream_threads(int cpl, bool reread = false) {
+  return reread ? kStreamRereadThreads : (cpl <= 4 ? 512 : SY_TUNE_STREAM8_THREADS);
 }
 
 // FULL: the row is exactly 32 * CPL chunks (D = 256, 512, 1024, 2048 bf16),
 // so no lane needs a validity predicate.
+
 template <typename T, int CPL, bool SOL, bool FULL>
 __global__ void __launch_bounds__(stream_threads(CPL), 1)
     stream_fwd_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
@@ -244,6 +254,196 @@ __global__ void __launch_bounds__(stream_threads(CPL), 1)
   }
 }
 
+// Re-read variant of the row stream (8 chunks per lane: 4 KiB rows). Per row,
+// pass 1 reads the lane's chunks from the row buffer for the dot and the sum
+// of squares only; after the online-softmax update pass 2 reads them again
+// for o (o += p * v_n; a new maximum first rescales o and enters v_n with
+// p = 1), and only then is the buffer refilled. The
+// fp32 row never lives in registers and the bookkeeping is kept to 32-bit
+// counters and one running source pointer, so 14 warps (128 registers) fit
+// on an SM: with whole tokens per warp that balances 28 tokens per SM as
+// 2 per warp (the representative 4096 tokens on 148 SMs).
+template <typename T, bool FULL>
+__global__ void __launch_bounds__(kStreamRereadThreads, 1)
+    stream_fwd_reread_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
+                             T* __restrict__ out, float* __restrict__ stats, const StreamCfg c) {
+  constexpr int CPL = 8;
+  constexpr int VEC = Dt<T>::kVec;
+  constexpr int P = VEC / 2;
+  const int RC = FULL ? 32 * CPL : c.row_chunks;  // chunks per row
+  const int RB = FULL ? 16 * 32 * CPL : c.row_bytes;
+  const StreamSmem L = stream_smem_layout(c);
+  float* wsm = reinterpret_cast<float*>(sy_smem + L.w_off);
+  unsigned char* ring0 = sy_smem + L.ring_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sy_smem + L.bar_off);
+  const unsigned char* zero_pad = sy_smem + L.zero_off;
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int wi = tid >> 5;
+  if (c.warps != (int)(blockDim.x >> 5) || c.ring < 1 || !c.reread) {
+    if (tid == 0) record_device_error(kDevErrBadPlan);
+    return;
+  }
+  if (tid == 0) {
+    for (int i = 0; i < c.warps * c.ring; ++i) mbar_init(&bars[i], 1);
+    *reinterpret_cast<uint4*>(sy_smem + L.zero_off) = make_uint4(0u, 0u, 0u, 0u);
+    mbar_fence_init();
+  }
+  for (int d = tid; d < c.D; d += blockDim.x) {
+    const int ch = d / VEC, e = d - ch * VEC;
+    wsm[((e >> 2) * c.row_chunks + ch) * 4 + (e & 3)] = load_any(w, w_dtype, d);
+  }
+  __syncthreads();
+
+  // This warp's tokens: tok0 + tstride * j, j < ntok (fewer than 2^31 rows
+  // per warp: the planner checks it).
+  const long long tstride = (long long)gridDim.x * c.warps;
+  const long long tok0 = blockIdx.x + (long long)gridDim.x * wi;
+  const int ntok = tok0 < c.BT ? (int)((c.BT - 1 - tok0) / tstride) + 1 : 0;
+  unsigned char* ring = ring0 + (size_t)wi * c.ring * RB;
+  uint64_t* bar = bars + wi * c.ring;
+  // next row to issue: source iss_n of the warp's token iss_j, at src
+  int iss_j = 0, iss_n = 0;
+  const unsigned char* src = reinterpret_cast<const unsigned char*>(v) + (size_t)tok0 * RB;
+  auto issue_next = [&](int slot_) {
+    if (iss_j >= ntok) return;
+    const size_t nstride = (size_t)c.BT * RB;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(&bar[slot_], (uint32_t)RB);
+      bulk_g2s(ring + (size_t)slot_ * RB, src, (uint32_t)RB, &bar[slot_], policy_evict_first());
+    }
+    if (++iss_n == c.N) {
+      iss_n = 0;
+      ++iss_j;
+      src += (size_t)gridDim.x * c.warps * RB - (size_t)(c.N - 1) * nstride;
+    } else {
+      src += nstride;
+    }
+  };
+  for (int s = 0; s < c.ring; ++s) issue_next(s);
+
+  auto cval = [&](int k) { return FULL || lane + 32 * k < RC; };
+  const float inv_d = 1.f / (float)c.D;
+  int slot = 0;
+  uint32_t ph = 0;
+  for (int j = 0; j < ntok; ++j) {
+    float2 o[CPL][P];
+#pragma unroll
+    for (int k = 0; k < CPL; ++k)
+#pragma unroll
+      for (int i = 0; i < P; ++i) o[k][i] = make_float2(0.f, 0.f);
+    // mref: the reference the weights are taken against (o and l hold
+    // sum exp(logit - mref) v and sum exp(logit - mref)); mx: the max logit.
+    float mref = 0.f, mx = 0.f, l = 0.f;
+    float lane_logit = 0.f, lane_r = 0.f;  // row `lane`'s statistics (lane < N)
+    float* st = stats != nullptr ? stats + (tok0 + tstride * j) * c.stats_stride : nullptr;
+    for (int n = 0; n < c.N; ++n) {
+      if (!mbar_wait(&bar[slot], ph)) return;
+      const unsigned char* row = ring + (size_t)slot * RB;
+      // pass 1: dot and sum of squares, two independent accumulator pairs each
+      constexpr int A = P < 2 ? P : 2;
+      float2 dacc[A], sacc[A];
+#pragma unroll
+      for (int i = 0; i < A; ++i) dacc[i] = sacc[i] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < CPL; ++k) {
+        if (k % 4 == 0 && k > 0) __syncwarp();  // bounds the loads hoisted ahead (registers)
+        float2 x[P];
+        unpack2<T>(lds128(cval(k) ? row + (lane + 32 * k) * 16 : zero_pad), x);
+        const float4* wp = reinterpret_cast<const float4*>(wsm) + (lane + 32 * k);
+#pragma unroll
+        for (int i = 0; i < P; i += 2) {
+          const float4 wv = cval(k) ? wp[(i / 2) * RC] : make_float4(0.f, 0.f, 0.f, 0.f);
+          dacc[0] = __ffma2_rn(make_float2(wv.x, wv.y), x[i], dacc[0]);
+          sacc[0] = __ffma2_rn(x[i], x[i], sacc[0]);
+          dacc[A - 1] = __ffma2_rn(make_float2(wv.z, wv.w), x[i + 1], dacc[A - 1]);
+          sacc[A - 1] = __ffma2_rn(x[i + 1], x[i + 1], sacc[A - 1]);
+        }
+      }
+#pragma unroll
+      for (int i = 1; i < A; ++i) {
+        dacc[0] = __fadd2_rn(dacc[0], dacc[i]);
+        sacc[0] = __fadd2_rn(sacc[0], sacc[i]);
+      }
+      // (dot, ssq) as one pair through the butterfly
+      float2 ds = make_float2(dacc[0].x + dacc[0].y, sacc[0].x + sacc[0].y);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+        ds = __fadd2_rn(ds, make_float2(__shfl_xor_sync(kFull, ds.x, off),
+                                        __shfl_xor_sync(kFull, ds.y, off)));
+      const float r = rsqrtf(ds.y * inv_d + c.eps);
+      const float logit = ds.x * r;
+      if (lane == (n & 31)) {
+        lane_logit = logit;
+        lane_r = r;
+      }
+      if (n >= 32 && st != nullptr && lane == 0) {  // rows past 32: written directly
+        st[n] = logit;
+        st[c.N + n] = r;
+      }
+      // Online softmax, warp-uniform (logit is bitwise equal in all lanes).
+      // Weights are exp(logit - mref); mref only moves when a logit exceeds it
+      // by more than kRescaleGap, so o is rescaled rarely and the weights stay
+      // below e^kRescaleGap (no overflow in fp32).
+      constexpr float kRescaleGap = 8.f;
+      float wgt = 1.f;
+      if (n == 0) {
+        mref = mx = logit;
+        l = 1.f;
+      } else {
+        mx = fmaxf(mx, logit);
+        if (logit > mref + kRescaleGap) {
+          const float sc = expf(mref - logit);
+          mref = logit;
+          l = fmaf(l, sc, 1.f);
+#pragma unroll
+          for (int k = 0; k < CPL; ++k)
+#pragma unroll
+            for (int i = 0; i < P; ++i) o[k][i] = __fmul2_rn(o[k][i], f2(sc));
+        } else {
+          wgt = expf(logit - mref);
+          l += wgt;
+        }
+      }
+      // pass 2: the row again, into o (o is 0 before the first row)
+#pragma unroll
+      for (int k = 0; k < CPL; ++k) {
+        if (k % 4 == 0 && k > 0) __syncwarp();
+        float2 x[P];
+        unpack2<T>(lds128(cval(k) ? row + (lane + 32 * k) * 16 : zero_pad), x);
+#pragma unroll
+        for (int i = 0; i < P; ++i) o[k][i] = __ffma2_rn(f2(wgt), x[i], o[k][i]);
+      }
+      __syncwarp();
+      if (lane == 0) fence_proxy_async();
+      issue_next(slot);
+      if (++slot == c.ring) {
+        slot = 0;
+        ph ^= 1u;
+      }
+    }
+    if (st != nullptr) {
+      if (lane < c.N) {
+        st[lane] = lane_logit;
+        st[c.N + lane] = lane_r;
+      }
+      if (lane == 0) {
+        st[2 * c.N] = mx;
+        st[2 * c.N + 1] = mref + logf(l);
+      }
+    }
+    const float inv = 1.f / l;
+    T* orow = out + (tok0 + tstride * j) * c.D;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+#pragma unroll
+      for (int i = 0; i < P; ++i) o[k][i] = __fmul2_rn(o[k][i], f2(inv));
+      if (cval(k)) stg128(orow + (lane + 32 * k) * VEC, pack2<T>(o[k]));
+    }
+  }
+}
+
 cudaError_t launch_stream_fwd(const StreamCfg& c, int grid, int cpl, int dtype, const void* v,
                               const void* w, int w_dtype, void* out, float* stats, bool sol,
                               cudaStream_t st);
@@ -255,6 +455,14 @@ cudaError_t launch_stream_tf(const StreamCfg& c, int grid, int cpl, const void* 
   const dim3 block(c.warps * 32);
   const T* vp = static_cast<const T*>(v);
   T* op = static_cast<T*>(out);
+  if (c.reread) {
+    if constexpr (!SOL) {
+      if (cpl == 8 && (int)block.x <= kStreamRereadThreads)
+        return launch_smem(stream_fwd_reread_kernel<T, FULL>, grid, block, smem, st, vp, w,
+                           w_dtype, op, stats, c);
+    }
+    return cudaErrorInvalidValue;
+  }
   switch (cpl) {
     case 1:
       return launch_smem(stream_fwd_kernel<T, 1, SOL, FULL>, grid, block, smem, st, vp, w, w_dtype,

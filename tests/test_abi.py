@@ -124,9 +124,13 @@ def test_planner_invariants_for_b200(native, dtype_name):
                     assert op == 0 and p["threads_per_group"] == 32
                     assert p["chunks_per_thread"] * 32 * 16 >= d * dt.itemsize
                     assert p["groups"] * 32 <= 512 and p["stages"] >= 2
+    # representative forward: re-read row stream, 14 warps x 2 whole tokens each
+    # (28 tokens per SM), at least 3 row buffers per warp
     rep = native.plan_info(0, 9, 4096, 2048, 1, torch.bfloat16, **B200)
-    assert rep["kind"] == 1 and rep["stages"] >= 4  # register tile, >= 4 tokens in flight
+    assert rep["kind"] == 3 and rep["groups"] == 14 and rep["stages"] >= 3
+    assert rep["grid"] * rep["groups"] * 2 >= 4096
     assert native.plan_info(0, 17, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 3
+    assert native.plan_info(0, 9, 4096, 512, 1, torch.bfloat16, **B200)["kind"] == 1
     assert native.plan_info(1, 9, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 1
     # rows that are not a multiple of 16 bytes go to the generic kernels
     assert native.plan_info(0, 3, 64, 777, 1, torch.bfloat16, **B200)["kind"] == 0

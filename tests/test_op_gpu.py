@@ -23,7 +23,14 @@ from switchyard import (  # noqa: E402
     speed_of_light,
 )
 from switchyard import _native  # noqa: E402
-from switchyard.triton_op import DEFAULT_EPS, PLAN_GENERIC, PLAN_STREAM, PLAN_TILE, _plan  # noqa: E402
+from switchyard.triton_op import (  # noqa: E402
+    DEFAULT_EPS,
+    PLAN_GENERIC,
+    PLAN_SMEM_TILE,
+    PLAN_STREAM,
+    PLAN_TILE,
+    _plan,
+)
 
 DEV = "cuda"
 
@@ -148,11 +155,14 @@ def test_batched_rejects_gradients_and_bad_inputs():
 def test_dispatch_sends_the_representative_shape_to_the_tile_kernels():
     """tests/test_triton_op.py:271-288: N=9, D=2048 is the shape a Block
     AttnRes model spends most of its time in; pin its path."""
-    assert _plan("fwd", 9, 4096, 2048, torch.bfloat16) == PLAN_TILE
+    # 4 KiB rows: the re-read row-stream forward, the register-tile backward
+    assert _plan("fwd", 9, 4096, 2048, torch.bfloat16) == PLAN_STREAM
     assert _plan("bwd", 9, 4096, 2048, torch.bfloat16) == PLAN_TILE
     for n in range(1, 10):  # every source count the 24-layer 8-block model uses
-        assert _plan("fwd", n, 8192, 2048, torch.bfloat16) == PLAN_TILE
+        assert _plan("fwd", n, 8192, 2048, torch.bfloat16) == PLAN_STREAM
         assert _plan("bwd", n, 8192, 2048, torch.bfloat16) == PLAN_TILE
+    # shorter rows: the register-tile forward
+    assert _plan("fwd", 9, 4096, 512, torch.bfloat16) == PLAN_TILE
     # more sources than the register tile holds: the row-stream forward
     assert _plan("fwd", 17, 4096, 2048, torch.bfloat16) == PLAN_STREAM
     # rows that are not a multiple of 16 bytes take the generic kernels
@@ -161,6 +171,41 @@ def test_dispatch_sends_the_representative_shape_to_the_tile_kernels():
 
 
 # ---------------------------------------------------------------- edge cases
+
+
+EPS_SHAPES = [  # fp32 shapes that reach every kernel family
+    ((9, 1, 64, 1024), PLAN_STREAM, PLAN_TILE),  # 4 KiB rows: re-read row stream
+    ((7, 2, 16, 512), PLAN_TILE, PLAN_TILE),
+    ((9, 1, 48, 256), PLAN_TILE, PLAN_TILE),
+    ((17, 1, 40, 1024), PLAN_STREAM, PLAN_SMEM_TILE),
+    ((10, 1, 24, 2048), PLAN_SMEM_TILE, PLAN_SMEM_TILE),
+    ((3, 1, 16, 777), PLAN_GENERIC, PLAN_GENERIC),
+]
+
+
+@pytest.mark.parametrize("eps", [DEFAULT_EPS, 0.25])
+@pytest.mark.parametrize("shape,fwd_kind,bwd_kind", EPS_SHAPES)
+def test_eps_reaches_every_kernel(shape, fwd_kind, bwd_kind, eps):
+    """eps is an argument of every kernel, not a constant: a source row of
+    zeros gets r = eps**-1/2 and logit 0 (not NaN), and a large eps changes
+    every logit (reference.py:98-104)."""
+    n, b, t, d = shape
+    assert _plan("fwd", n, b * t, d, torch.float32) == fwd_kind
+    assert _plan("bwd", n, b * t, d, torch.float32) == bwd_kind
+    v = randn(*shape, seed=21)
+    v[2, :, ::3] = 0.0  # every third token has an all-zero source 2
+    w = randn(d, seed=22) / d**0.5
+    g = randn(b, t, d, seed=23)
+    v = v.detach().requires_grad_(True)
+    w = w.detach().requires_grad_(True)
+    out = block_attn_res_triton(v, w, eps)
+    out.backward(g)
+    assert torch.isfinite(out).all() and torch.isfinite(v.grad).all()
+    np.testing.assert_allclose(np64(out), O.forward(np64(v), np64(w), eps), rtol=2e-5, atol=2e-6)
+    dv_o, dw_o = O.backward(np64(v), np64(w), np64(g), eps)
+    np.testing.assert_allclose(np64(v.grad), dv_o, rtol=2e-4, atol=2e-5)
+    # dw sums B*T tokens: absolute error scales with its largest entries
+    np.testing.assert_allclose(np64(w.grad), dw_o, rtol=2e-4, atol=2e-6 * np.abs(dw_o).max())
 
 
 def test_empty_token_axis():
