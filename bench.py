@@ -189,7 +189,7 @@ class L2Flush:
         torch.sum(self.r, dim=0, out=self.o)
 
 
-def timed_steps(fn, steps, flush, lead_cycles=400_000):
+def timed_steps(fn, steps, flush, lead_cycles=2_000_000):
     """Per-step device times (ms): flush L2, let a spin kernel cover the host's
     queueing of the step, then bracket only the step with CUDA events on the
     current stream."""
@@ -206,14 +206,19 @@ def timed_steps(fn, steps, flush, lead_cycles=400_000):
 
 
 def summarize(ms):
-    ms = sorted(ms)
-    n = len(ms)
+    order = sorted(ms)
+    n = len(order)
+    med = order[n // 2]
+    slow = [i for i, x in enumerate(ms) if x > 1.2 * med]
     return {
-        "mean_ms": statistics.fmean(ms),
-        "median_ms": ms[n // 2],
-        "p10_ms": ms[max(0, int(0.1 * n))],
-        "p90_ms": ms[min(n - 1, int(0.9 * n))],
-        "min_ms": ms[0],
+        "mean_ms": statistics.fmean(order),
+        "median_ms": med,
+        "p10_ms": order[max(0, int(0.1 * n))],
+        "p90_ms": order[min(n - 1, int(0.9 * n))],
+        "min_ms": order[0],
+        "max_ms": order[-1],
+        # steps more than 20 % above the median, by position in the timed sequence
+        "slow_steps": {"count": len(slow), "first_indices": slow[:8]},
     }
 
 
@@ -431,7 +436,7 @@ def run_ours(args):
             "step_stats": st_step,
             "fwd_stats": st_fwd,
             "roofline": {
-                "kernel": "tile_bwd_kernel (sy_bwd)",
+                "kernel": kernel_label(_native, "bwd", n, b * t, d),
                 "bound": "hbm",
                 "achieved": bwd_ach,
                 "peak": peak,
@@ -442,7 +447,7 @@ def run_ours(args):
                 "traffic": traffic.get("bwd"),
             },
             "roofline_fwd": {
-                "kernel": "tile_fwd_kernel (sy_fwd)",
+                "kernel": kernel_label(_native, "fwd", n, b * t, d),
                 "bound": "hbm",
                 "achieved": fwd_ach,
                 "peak": peak,
@@ -476,6 +481,25 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)
+
+
+def kernel_label(native, op: str, n: int, bt: int, d: int) -> str:
+    """Name of the kernel the C ABI plans for this shape (sy_plan_info)."""
+    code = {"fwd": 0, "bwd": 1}[op]
+    info = native.plan_info(code, n, bt, d, 1, torch.bfloat16)
+    kind = info["kind"]
+    if kind == 3:
+        name = "stream_fwd_reread_kernel" if info["chunks_per_thread"] == 8 else "stream_fwd_kernel"
+        shape = f"row stream, {info['groups']} warps x 1 token, {info['stages']} row buffers/warp"
+    elif kind == 1:
+        name = f"reg_{op}_kernel"
+        shape = (f"register tile, {info['groups']} groups x {info['threads_per_group'] // 32} warps, "
+                 f"{info['chunks_per_thread']} chunk/thread, {info['stages']} stages")
+    elif kind == 2:
+        name, shape = f"tile_{op}_kernel", "shared-memory tile"
+    else:
+        name, shape = f"gen_{op}_kernel", "generic"
+    return f"{name} (sy_{op}; {shape})"
 
 
 def read_traffic():
