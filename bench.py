@@ -460,7 +460,8 @@ def run_ours(args):
             },
             "kernels_ms": {k: v_["mean_ms"] for k, v_ in kt.items()},
             "dw_partial_rows": p_rows,
-            "gpu_launches": 3 * args.steps,
+            # per step: forward, backward, dw reduction (+ the peer dw exchange on N > 1)
+            "gpu_launches": (3 if world == 1 else 4) * args.steps,
             "clocks": sampler.summary(),
         }
     if not args.no_extras and rank == 0:

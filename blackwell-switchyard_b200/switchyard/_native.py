@@ -43,6 +43,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sy_device_error": ([_c.POINTER(_c.c_int)], _I),
     "sy_bwd_noalloc": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _F, _P], _I),
     "sy_bwd_noalloc_max_floats": ([], _I64),
+    "sy_dw_exchange": ([_P, _I, _I, _I64, _I64, _c.c_uint32, _I64, _P, _I, _P], _I),
 }
 
 
@@ -175,3 +176,15 @@ def device_error() -> int:
     code = ctypes.c_int(0)
     check(lib.sy_device_error(ctypes.byref(code)), "sy_device_error")
     return code.value
+
+
+def dw_exchange(peer_bases, world: int, rank: int, slot_off: int, flag_off: int, tag: int,
+                dw) -> None:
+    """Rank-order sum of the ranks' fp32 dw slots into ``dw`` (sy_dw_exchange);
+    ``peer_bases`` is a CUDA int64 tensor of the ranks' buffer addresses."""
+    check(
+        lib.sy_dw_exchange(peer_bases.data_ptr(), world, rank, slot_off, flag_off,
+                           tag & 0xFFFFFFFF, dw.numel(), dw.data_ptr(), dtype_code(dw.dtype),
+                           stream_of(dw)),
+        "sy_dw_exchange",
+    )

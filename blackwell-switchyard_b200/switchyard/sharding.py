@@ -6,17 +6,28 @@ Every token ``(b, t)`` is independent for ``out``, ``dv`` and the softmax
 its own ``v[:, range]`` as a ``[N, B_local*T_local, D]`` allocation: no input
 exchange and no exchange for ``out`` or ``dv``. The only quantity that crosses
 GPUs is the query gradient ``dw = sum over all tokens``: each rank reduces its
-own fp32 partial, the D-length rows are all-gathered (8 KiB at D=2048, NCCL
-over NVLink on GPUs, gloo in the CPU tests) and every rank adds them in rank
-order 0..world-1, so all ranks hold the bitwise-same ``dw`` and the result is
+own fp32 partial and every rank adds all ranks' partials in rank order
+0..world-1, so all ranks hold the bitwise-same ``dw`` and the result is
 deterministic for a given partition.
+
+On CUDA ranks the partials cross NVLink as peer loads: each rank's dw
+reduction writes into a buffer every rank can address (torch symmetric memory,
+allocated once per group and D), and one kernel (``sy_dw_exchange``) announces,
+waits for all ranks with a bounded wait, and sums the peers' rows directly --
+no NCCL call on the step. Elsewhere (gloo on CPU, or if peer memory is not
+available, or with ``SWITCHYARD_DW_EXCHANGE=collective``) the rows are
+all-gathered with the process group and summed in the same order, which gives
+the same bits.
 """
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
+from . import _native
 from .triton_op import DEFAULT_EPS, _backward, _forward, _validate
 
 __all__ = ["token_range", "exchange_dw", "block_attn_res_sharded"]
@@ -46,6 +57,71 @@ def exchange_dw(dw_local: torch.Tensor, group=None) -> torch.Tensor:
     return total
 
 
+class _PeerDw:
+    """The peer-memory dw exchange of one (process group, D, device): a buffer
+    every rank can address -- two fp32 slots of D floats, used alternately,
+    and one uint32 flag per rank -- and the device array of all ranks'
+    addresses of it. Built collectively on first use."""
+
+    def __init__(self, group, d: int, device: torch.device):
+        import torch.distributed._symmetric_memory as symm
+
+        group = group if group is not None else dist.group.WORLD
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.d = d
+        self.slot_floats = (d + 3) // 4 * 4  # keeps the second slot 16-byte aligned
+        flag_floats = (self.world + 3) // 4 * 4
+        self.buf = symm.empty(2 * self.slot_floats + flag_floats, dtype=torch.float32,
+                              device=device)
+        self.buf.zero_()
+        self.handle = symm.rendezvous(self.buf, group)
+        ptrs = list(self.handle.buffer_ptrs)
+        delta = self.buf.data_ptr() - ptrs[self.rank]
+        self.bases = torch.tensor([p + delta for p in ptrs], dtype=torch.int64, device=device)
+        self.flag_off = 2 * self.slot_floats * 4
+        self.tag = 0
+        torch.cuda.synchronize(device)
+        dist.barrier(group)  # every rank's flags are zero before the first announcement
+
+    def next_slot(self):
+        """The slot this call's local dw goes into, and its byte offset."""
+        self.tag += 1
+        off = (self.tag & 1) * self.slot_floats
+        return self.buf[off: off + self.d], off * 4
+
+    def exchange(self, slot_off: int, dw: torch.Tensor) -> None:
+        _native.dw_exchange(self.bases, self.world, self.rank, slot_off, self.flag_off,
+                            self.tag, dw)
+
+
+_PEER: dict = {}
+_PEER_UNAVAILABLE: set = set()
+
+
+def _peer_dw(group, d: int, device: torch.device):
+    """The group's peer exchange for D, or None where the collective path is used."""
+    if device.type != "cuda" or os.environ.get("SWITCHYARD_DW_EXCHANGE") == "collective":
+        return None
+    world = dist.get_world_size(group)
+    if world < 2:
+        return None
+    gname = (group or dist.group.WORLD).group_name
+    key = (gname, d, device.index)
+    if key in _PEER_UNAVAILABLE:
+        return None
+    peer = _PEER.get(key)
+    if peer is None:
+        try:
+            peer = _PEER[key] = _PeerDw(group, d, device)
+        except (RuntimeError, ImportError, AttributeError):
+            # every rank takes the same branch: the allocation or the
+            # rendezvous is unsupported on this system
+            _PEER_UNAVAILABLE.add(key)
+            return None
+    return peer
+
+
 class _ShardedBlockAttnRes(torch.autograd.Function):
     """Local forward on this rank's tokens; backward adds the ranks' dw."""
 
@@ -60,8 +136,15 @@ class _ShardedBlockAttnRes(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out):
         v, w, stats = ctx.saved_tensors
-        dv, dw32 = _backward(v, w, stats, grad_out, ctx.eps, torch.float32)
-        dw = exchange_dw(dw32, ctx.group).to(w.dtype)
+        peer = _peer_dw(ctx.group, w.shape[0], w.device)
+        if peer is not None:
+            slot, off = peer.next_slot()
+            dv, _ = _backward(v, w, stats, grad_out, ctx.eps, torch.float32, dw_out=slot)
+            dw = torch.empty_like(w)
+            peer.exchange(off, dw)
+        else:
+            dv, dw32 = _backward(v, w, stats, grad_out, ctx.eps, torch.float32)
+            dw = exchange_dw(dw32, ctx.group).to(w.dtype)
         return dv, dw, None, None
 
 

@@ -103,15 +103,16 @@ def _forward(v: torch.Tensor, w: torch.Tensor, eps: float):
     return v, w, out, stats, strategy
 
 
-def _backward(v, w, stats, grad_out, eps: float, dw_dtype: torch.dtype):
+def _backward(v, w, stats, grad_out, eps: float, dw_dtype: torch.dtype, dw_out=None):
     """Launch the backward and the fixed-order dw reduction. Returns
     ``(dv, dw)`` with ``dw`` in ``dw_dtype`` (float32 for the sharded path,
-    which still has to add the other ranks' contributions)."""
+    which still has to add the other ranks' contributions), written into
+    ``dw_out`` when one is given."""
     n, b, t, d = v.shape
     bt = b * t
     g = grad_out.to(v.dtype).contiguous()
     dv = torch.empty_like(v)
-    dw = torch.empty(d, device=v.device, dtype=dw_dtype)
+    dw = torch.empty(d, device=v.device, dtype=dw_dtype) if dw_out is None else dw_out
     if d == 0:
         return dv, dw
     with torch.cuda.device(v.device):

@@ -176,6 +176,27 @@ SY_API int sy_bwd_noalloc(const void* v, const void* w, const void* g,
 SY_API int64_t sy_bwd_noalloc_max_floats(void);
 
 /*
+ * Cross-GPU sum of token-sharded dw (one call per rank, each on its own GPU).
+ * Replaces the data-parallel gradient all-reduce of w that the reference leaves
+ * to DDP (bench/bench_ddp.py:49,65); the op itself has no multi-GPU code.
+ *
+ * Every rank owns a buffer that all ranks can address (NVLink peer mappings),
+ * laid out as two fp32 slots of D floats at slot_off and slot_off + slot stride
+ * chosen by the caller, and `world` uint32 flags at flag_off; peer_bases is a
+ * DEVICE array of `world` 64-bit addresses, entry r = rank r's buffer base.
+ * Before the call the rank's own fp32 dw must be in its slot (slot_off already
+ * selects slot tag & 1) by earlier work on `stream`. The kernel announces `tag`
+ * to every rank, waits (bounded, 2 s; a timeout sets the device error word) for
+ * all ranks' announcements, then writes dw[D] in dw_dtype = sum over ranks
+ * 0..world-1, in that order, of their slots -- bitwise the same on every rank.
+ * Tags must increase by one per call, the same sequence on every rank; flags
+ * start at 0. Plain peer loads only (no multicast).
+ */
+SY_API int sy_dw_exchange(const void* peer_bases, int world, int rank, int64_t slot_off,
+                          int64_t flag_off, uint32_t tag, int64_t D, void* dw, int dw_dtype,
+                          sy_stream_t stream);
+
+/*
  * Reads the device-side error word of the current device and clears it.
  * Synchronises the device. Bit 1: a kernel's bounded wait ran out; bit 2: a
  * kernel refused an inconsistent launch plan. Writes 0 to *code when no error

@@ -82,6 +82,12 @@ def test_host_validation_rejects_bad_arguments(native):
     assert L.sy_dw_reduce(None, 1, 0, None, bf16, None) == native.SY_OK
     assert L.sy_bwd_partials(3, 0, 16, bf16) == 1
     assert L.sy_bwd_partials(0, 4, 16, bf16) < 0
+    # dw exchange: rank outside the world, misaligned slot, bad world size, dtype
+    assert L.sy_dw_exchange(1, 2, 2, 0, 64, 1, 8, 1, bf16, None) == native.SY_ERR_ARG
+    assert L.sy_dw_exchange(1, 2, 0, 8, 64, 1, 8, 1, bf16, None) == native.SY_ERR_ARG
+    assert L.sy_dw_exchange(1, 0, 0, 0, 64, 1, 8, 1, bf16, None) == native.SY_ERR_ARG
+    assert L.sy_dw_exchange(1, 2, 0, 0, 64, 1, 8, 1, bad, None) == native.SY_ERR_DTYPE
+    assert L.sy_dw_exchange(None, 2, 0, 0, 64, 1, 0, None, bf16, None) == native.SY_OK
 
 
 B200 = dict(sms=148, max_smem=232448)  # multiprocessors, opt-in shared memory per block
