@@ -87,6 +87,15 @@ def load_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def load_peak_field(name: str):
+    """A field of MEASURED_PEAKS.json, or None."""
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        v = json.loads(p.read_text()).get(name)
+        return float(v) if v is not None else None
+    return None
+
+
 def alg_bytes(n, b, t, d, itemsize=ITEM):
     fwd = (n + 1) * b * t * d * itemsize
     bwd = (2 * n + 1) * b * t * d * itemsize
@@ -292,10 +301,17 @@ def kernel_times(native, v, w, dout, steps, flush, stream):
     return res, p
 
 
-def batched_times(v, steps, flush, qs=(1, 4, 8, 16)):
+def batched_times(v, steps, flush, hbm_gbs, qs=(1, 4, 8, 16)):
+    """block_attn_res_batched at Q queries. Roofline: the larger of the HBM time
+    (algorithmic bytes at the measured copy bandwidth) and the FP32 time
+    ((2+4Q)*N*BT*D FLOP at the device's nominal FP32 FMA rate, SMs x 128 lanes x
+    2 FLOP x the maximum SM clock), naming which one binds."""
     from switchyard import block_attn_res_batched
 
     n, b, t, d = v.shape
+    props = torch.cuda.get_device_properties(v.device)
+    clock_mhz = load_peak_field("sm_max_mhz") or 1965.0
+    fp32_tflops = props.multi_processor_count * 128 * 2 * clock_mhz * 1e6 / 1e12
     out = {}
     gen = torch.Generator(device=v.device).manual_seed(7)
     for q in qs:
@@ -310,6 +326,16 @@ def batched_times(v, steps, flush, qs=(1, 4, 8, 16)):
         s["tbps"] = byts / (s["mean_ms"] * 1e-3) / 1e12
         s["bytes"] = byts
         s["flops"] = flops
+        t_hbm = byts / (hbm_gbs * 1e9) * 1e3
+        t_fp32 = flops / (fp32_tflops * 1e12) * 1e3
+        s["roofline"] = {
+            "bound": "hbm" if t_hbm >= t_fp32 else "fp32",
+            "roofline_ms": max(t_hbm, t_fp32),
+            "hbm_ms": t_hbm,
+            "fp32_ms": t_fp32,
+            "fp32_tflops_nominal": fp32_tflops,
+            "frac": max(t_hbm, t_fp32) / s["mean_ms"],
+        }
         out[f"Q{q}"] = s
     return out
 
@@ -465,7 +491,7 @@ def run_ours(args):
             "clocks": sampler.summary(),
         }
     if not args.no_extras and rank == 0:
-        result["batched"] = batched_times(v, max(20, args.steps // 4), flush)
+        result["batched"] = batched_times(v, max(20, args.steps // 4), flush, peak)
         e2e, h2d, d2h = e2e_times(dev, 10, n, b, t, d, block_attn_res_triton)
         result["e2e"] = {
             "value": tot_b / (e2e["mean_ms"] * 1e-3) / 1e12,

@@ -7,6 +7,7 @@
 #include <cstring>
 #include <mutex>
 
+#include "sy_batched.cuh"
 #include "sy_reg.cuh"
 #include "sy_stream.cuh"
 #include "sy_tile.cuh"
@@ -277,6 +278,62 @@ StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInf
   return p;
 }
 
+// Batched-query register tile: the fp32 tile (N * CPT * VEC floats per thread)
+// must fit kBatchedTileFloats; as many chunks per thread as fit (fewer warps
+// per token: less reduction work per query), groups of up to 256 threads, the
+// queries' S rows in shared memory beside the ring.
+TilePlan plan_batched(int64_t N, int64_t BT, int64_t D, int64_t S, int dtype, const DevInfo& di) {
+  TilePlan p;
+  const int es = esize_of(dtype);
+  if (!es || N < 1 || N > kRegMaxN || S < 2 || S > kBatchedMaxS || D < 1 || D > kMaxD ||
+      BT < 1 || BT > INT_MAX)
+    return p;
+  if ((D * es) % 16) return p;
+  const int vec = 16 / es;
+  const int64_t rc = D * es / 16;
+  int cpt = 0, tg = 0;
+  for (int cand = 4; cand >= 1 && !cpt; cand /= 2) {
+    if (N * cand * vec > kBatchedTileFloats) continue;
+    if (cand > 1 && rc < 32 * cand) continue;  // lanes would be idle
+    const int64_t t = round32((rc + cand - 1) / cand);
+    if (t <= 256 && (rc + t - 1) / t <= cand) cpt = cand, tg = (int)t;
+  }
+  if (!cpt) return p;
+  TileCfg c{};
+  c.BT = BT;
+  c.N = (int)N;
+  c.D = (int)D;
+  c.row_chunks = (int)rc;
+  c.row_bytes = (int)(D * es);
+  c.stats_stride = (int)stats_stride(N);
+  c.red_stride = tile_red_stride((int)N);
+  c.coef_stride = 2 * kRegMaxN;  // alpha as fp32 pairs, one slot per warp
+  c.tg = tg;
+  DevInfo room = di;  // the queries take S rows of shared memory
+  room.max_smem = di.max_smem - (int)(S * c.row_bytes) - 128;
+  int64_t smem = 0;
+  if (room.max_smem <= 0 || !size_ring(c, kOpFwd, 256 / tg, room, &smem, true)) return p;
+  p.kind = kPlanRegTile;
+  p.c = c;
+  p.cpt = cpt;
+  p.grid = (int)(BT < di.sms ? BT : di.sms);
+  p.smem = (int64_t)(batched_q_off(c) + (size_t)S * c.row_bytes);
+  return p;
+}
+
+cudaError_t launch_plan_batched(const TilePlan& p, int S, int dtype, const void* v,
+                                const void* q, void* out, cudaStream_t st) {
+  switch (dtype) {
+    case SY_BF16:
+      return launch_batched_bf16(p.c, p.grid, p.cpt, S, v, q, out, st);
+    case SY_F16:
+      return launch_batched_f16(p.c, p.grid, p.cpt, S, v, q, out, st);
+    case SY_F32:
+      return launch_batched_f32(p.c, p.grid, p.cpt, S, v, q, out, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
 cudaError_t launch_plan_fwd(const TilePlan& p, int dtype, const void* v, const void* w,
                             int w_dtype, void* out, float* stats, cudaStream_t st) {
   if (p.kind == kPlanRegTile) {
@@ -478,6 +535,12 @@ int sy_fwd_batched(const void* v, const void* queries, void* out, int64_t N, int
   DevInfo di;
   cudaError_t e = dev_info(&di);
   if (e != cudaSuccess) return cuda_status(e, "sy_fwd_batched: device query");
+  TilePlan bp = plan_batched(N, BT, D, S, dtype, di);
+  bp.c.eps = eps;
+  if (bp.kind == kPlanRegTile && al16(v) && al16(queries) && al16(out)) {
+    e = launch_plan_batched(bp, (int)S, dtype, v, queries, out, static_cast<cudaStream_t>(stream));
+    return cuda_status(e, "sy_fwd_batched: register-tile kernel launch");
+  }
   if (!generic_batched_fits(N, S, di)) return SY_ERR_UNSUPPORTED;
   e = launch_generic_batched(BT, (int)N, (int)D, (int)S, dtype, v, queries, out, eps,
                              generic_grid(BT, di), static_cast<cudaStream_t>(stream));
@@ -542,7 +605,10 @@ int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype,
     }
   }
   TilePlan p;
-  if (op != 2 || S == 1) p = plan_tile(top, N, bt, D, dtype, di);
+  if (op != 2 || S == 1)
+    p = plan_tile(top, N, bt, D, dtype, di);
+  else
+    p = plan_batched(N, bt, D, S, dtype, di);
   out[0] = p.kind;
   out[1] = p.grid;
   out[2] = p.c.stages;

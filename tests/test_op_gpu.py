@@ -165,6 +165,11 @@ def test_dispatch_sends_the_representative_shape_to_the_tile_kernels():
     assert _plan("fwd", 9, 4096, 512, torch.bfloat16) == PLAN_TILE
     # more sources than the register tile holds: the row-stream forward
     assert _plan("fwd", 17, 4096, 2048, torch.bfloat16) == PLAN_STREAM
+    # batched queries: the register tile reused across queries; tiles that do
+    # not fit registers (N=17, D=4096) take the generic kernel
+    for s in (2, 4, 8, 16):
+        assert _plan("batched", 9, 4096, 2048, torch.bfloat16, s) == PLAN_TILE
+    assert _plan("batched", 17, 4096, 4096, torch.bfloat16, 8) == PLAN_GENERIC
     # rows that are not a multiple of 16 bytes take the generic kernels
     assert _plan("fwd", 3, 64, 777, torch.bfloat16) == PLAN_GENERIC
     assert _plan("bwd", 5, 17, 63, torch.float32) == PLAN_GENERIC
