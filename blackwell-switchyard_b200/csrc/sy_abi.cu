@@ -306,8 +306,8 @@ TilePlan plan_batched(int64_t N, int64_t BT, int64_t D, int64_t S, int dtype, co
   c.row_chunks = (int)rc;
   c.row_bytes = (int)(D * es);
   c.stats_stride = (int)stats_stride(N);
-  c.red_stride = tile_red_stride((int)N);
-  c.coef_stride = 2 * kRegMaxN;  // alpha as fp32 pairs, one slot per warp
+  c.red_stride = 32;   // 32-value reductions (query blocks)
+  c.coef_stride = 64;  // alpha as fp32 pairs: up to 32 (query, source) pairs per warp
   c.tg = tg;
   DevInfo room = di;  // the queries take S rows of shared memory
   room.max_smem = di.max_smem - (int)(S * c.row_bytes) - 128;

@@ -10,10 +10,12 @@
 //
 //   * sums of squares of the N rows -> reduce-scatter over the warp, fixed-order
 //     sum over the group's warps through shared memory -> r_n, kept by lane n;
-//   * for each query s: dot_n = q_s . v_n from the registers (packed fp32 FMA),
-//     the same reduction, softmax over n in lanes 0..N-1, alpha_n published to
-//     the warp's own shared slot as fp32 pairs, and out[s] = sum_n alpha_n v_n
-//     written with one 16-byte store per chunk.
+//   * queries in blocks of QB (as many as fill a 32-value reduce-scatter: 3 at
+//     N = 9): dot_{s,n} = q_s . v_n from the registers (packed fp32 FMA), one
+//     reduction for the whole block, a softmax per query over its N lanes
+//     (segmented shuffles), alpha published to the warp's own shared slot as
+//     fp32 pairs, and out[s] = sum_n alpha_{s,n} v_n written with one 16-byte
+//     store per chunk.
 //
 // HBM traffic is the minimum ((N + S) rows per token); the work per token grows
 // with S, so large S is bound by FP32 issue rather than bandwidth.
@@ -37,7 +39,10 @@ __global__ void __launch_bounds__(256, 1)
                        const TileCfg c, int S) {
   constexpr int VEC = Dt<T>::kVec;
   constexpr int P = VEC / 2;
-  constexpr int M = 16;  // N <= 16 values per reduction
+  constexpr int M = 16;  // N <= 16 values per sum-of-squares reduction
+  // queries per reduction round: as many as fill the 32 values of one
+  // reduce-scatter (3 at N = 9), at most 4
+  constexpr int QB = (32 / N) < 1 ? 1 : ((32 / N) > 4 ? 4 : (32 / N));
   static_assert(N * CPT * VEC <= kBatchedTileFloats, "tile does not fit the register budget");
   const TileSmem L = tile_smem_layout(c);
   unsigned char* stage0 = sy_smem + L.stages_off;
@@ -54,8 +59,8 @@ __global__ void __launch_bounds__(256, 1)
   const int wpg = c.tg >> 5;
   const int nwc = c.groups * wpg;
 
-  if (c.N != N || c.groups < 1 || c.stages < c.groups || c.red_stride < M ||
-      c.coef_stride < 2 * N || S < 1 || S > kBatchedMaxS) {
+  if (c.N != N || c.groups < 1 || c.stages < c.groups || c.red_stride < 32 ||
+      c.coef_stride < 2 * QB * N || S < 1 || S > kBatchedMaxS) {
     if (tid == 0) record_device_error(kDevErrBadPlan);
     return;
   }
@@ -96,7 +101,8 @@ __global__ void __launch_bounds__(256, 1)
 
   // Sum M per-lane values over the group: reduce-scatter in the warp, then
   // the group's warps in order through shared memory. Every lane returns the
-  // total of value lane >> 1. `k` counts the reductions (buffer parity).
+  // total of value lane >> 1 (lane, for the 32-value form). `k` counts the
+  // reductions (buffer parity).
   int k = 0;
   auto group_reduce = [&](float (&a)[M]) {
     const float tl = warp_reduce_scatter<M>(a, lane);
@@ -109,6 +115,19 @@ __global__ void __launch_bounds__(256, 1)
       __syncwarp();
     float tot = 0.f;
     for (int w = 0; w < wpg; ++w) tot += red[(cw0 + w) * c.red_stride + (lane >> 1)];
+    return tot;
+  };
+  auto group_reduce32 = [&](float (&a)[32]) {
+    const float tl = warp_reduce_scatter<32>(a, lane);
+    float* red = red_base + (size_t)(k & 1) * nwc * c.red_stride;
+    ++k;
+    red[cw * c.red_stride + lane] = tl;
+    if (wpg > 1)
+      named_sync(1 + g, c.tg);
+    else
+      __syncwarp();
+    float tot = 0.f;
+    for (int w = 0; w < wpg; ++w) tot += red[(cw0 + w) * c.red_stride + lane];
     return tot;
   };
 
@@ -158,61 +177,82 @@ __global__ void __launch_bounds__(256, 1)
       r_l = rsqrtf(__shfl_sync(kFull, tot, 2 * ln) * inv_d + c.eps);
     }
 
-    // ---- one query at a time, from the registers ----
-    for (int s = 0; s < S; ++s) {
-      float a[M];
+    // ---- queries in blocks of QB, from the registers ----
+    for (int s0 = 0; s0 < S; s0 += QB) {
+      const int qb = S - s0 < QB ? S - s0 : QB;  // queries in this block (warp-uniform)
+      // value qi*N + n = q_{s0+qi} . v_n (this thread's part)
+      float a[32];
 #pragma unroll
-      for (int i = 0; i < M; ++i) a[i] = 0.f;
+      for (int i = 0; i < 32; ++i) a[i] = 0.f;
 #pragma unroll
-      for (int cc = 0; cc < CPT; ++cc) {
-        float2 qf[P];
-        unpack2<T>(cv[cc] ? lds128(qsm + (size_t)s * c.row_bytes + (tig + cc * c.tg) * 16)
-                          : make_uint4(0u, 0u, 0u, 0u),
-                   qf);
+      for (int qi = 0; qi < QB; ++qi) {
+        if (qi < qb) {
+          float2 acc[N];
 #pragma unroll
-        for (int n = 0; n < N; ++n) {
-          float2 p[P];
-          x.get(n, cc, p);
-          float2 acc = make_float2(0.f, 0.f);
+          for (int n = 0; n < N; ++n) acc[n] = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int i = 0; i < P; ++i) acc = __ffma2_rn(qf[i], p[i], acc);
-          a[n] += acc.x + acc.y;
+          for (int cc = 0; cc < CPT; ++cc) {
+            float2 qf[P];
+            unpack2<T>(cv[cc] ? lds128(qsm + (size_t)(s0 + qi) * c.row_bytes +
+                                       (tig + cc * c.tg) * 16)
+                              : make_uint4(0u, 0u, 0u, 0u),
+                       qf);
+#pragma unroll
+            for (int n = 0; n < N; ++n) {
+              float2 p[P];
+              x.get(n, cc, p);
+#pragma unroll
+              for (int i = 0; i < P; ++i) acc[n] = __ffma2_rn(qf[i], p[i], acc[n]);
+            }
+          }
+#pragma unroll
+          for (int n = 0; n < N; ++n) a[qi * N + n] = acc[n].x + acc[n].y;
         }
       }
-      const float tot = group_reduce(a);
-      const int ln = lane < N ? lane : 0;
-      // every lane takes part in the shuffle (full mask); only then select
-      const float dot = __shfl_sync(kFull, tot, 2 * ln);
-      const float logit = lane < N ? dot * r_l : -INFINITY;
-      const float m = warp_max(logit);
-      const float e = lane < N ? expf(logit - m) : 0.f;
-      const float l = warp_sum(e);
+      // lane L: the group total of value L
+      const float tot = group_reduce32(a);
+      // softmax over the N sources of each query: lanes qi*N .. qi*N+N-1
+      const bool act = lane < qb * N;
+      const int qi = act ? lane / N : 0;
+      const int n = act ? lane - qi * N : 0;
+      const int base = qi * N;
+      // every lane takes part in each shuffle (full mask); selects come after
+      const float r_n = __shfl_sync(kFull, r_l, n);
+      const float logit = act ? tot * r_n : -INFINITY;
+      float m = -INFINITY;
+#pragma unroll
+      for (int jj = 0; jj < N; ++jj) m = fmaxf(m, __shfl_sync(kFull, logit, base + jj));
+      const float e = act ? expf(logit - m) : 0.f;
+      float l = 0.f;
+#pragma unroll
+      for (int jj = 0; jj < N; ++jj) l += __shfl_sync(kFull, e, base + jj);
       const float al = e / l;
-      __syncwarp();  // the previous query's reads of the slot are done
-      if (lane < N) reinterpret_cast<float2*>(alpha_slot)[lane] = make_float2(al, al);
+      __syncwarp();  // the previous block's reads of the slot are done
+      if (act) reinterpret_cast<float2*>(alpha_slot)[lane] = make_float2(al, al);
       __syncwarp();
-      float2 alp[N];
 #pragma unroll
-      for (int n = 0; n < N; n += 2) {
-        const float4 pr = alpha_slot[n / 2];
-        alp[n] = make_float2(pr.x, pr.y);
-        if (n + 1 < N) alp[n + 1] = make_float2(pr.z, pr.w);
-      }
-      T* orow = out + ((size_t)s * c.BT + tok) * c.D;
+      for (int qo = 0; qo < QB; ++qo) {
+        if (qo < qb) {
+          float2 alp[N];
 #pragma unroll
-      for (int cc = 0; cc < CPT; ++cc) {
-        if (!cv[cc]) continue;
-        float2 o[P];
+          for (int k2 = 0; k2 < N; ++k2) alp[k2] = reinterpret_cast<const float2*>(alpha_slot)[qo * N + k2];
+          T* orow = out + ((size_t)(s0 + qo) * c.BT + tok) * c.D;
 #pragma unroll
-        for (int i = 0; i < P; ++i) o[i] = make_float2(0.f, 0.f);
+          for (int cc = 0; cc < CPT; ++cc) {
+            if (!cv[cc]) continue;
+            float2 o[P];
 #pragma unroll
-        for (int n = 0; n < N; ++n) {
-          float2 p[P];
-          x.get(n, cc, p);
+            for (int i = 0; i < P; ++i) o[i] = make_float2(0.f, 0.f);
 #pragma unroll
-          for (int i = 0; i < P; ++i) o[i] = __ffma2_rn(alp[n], p[i], o[i]);
+            for (int k2 = 0; k2 < N; ++k2) {
+              float2 p[P];
+              x.get(k2, cc, p);
+#pragma unroll
+              for (int i = 0; i < P; ++i) o[i] = __ffma2_rn(alp[k2], p[i], o[i]);
+            }
+            stg128(orow + (size_t)(tig + cc * c.tg) * VEC, pack2<T>(o));
+          }
         }
-        stg128(orow + (size_t)(tig + cc * c.tg) * VEC, pack2<T>(o));
       }
     }
 
