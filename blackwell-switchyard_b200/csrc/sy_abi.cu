@@ -238,8 +238,11 @@ StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInf
   if (!es || N < 1 || D < 1 || D > kMaxD || BT < 1 || BT > INT_MAX) return p;
   if ((D * es) % 16) return p;
   const int64_t rc = D * es / 16;
+  // Rows of exactly 2 or 4 times 4 KiB: the split re-read kernel, K warps per
+  // token. Otherwise one warp per token, rows of at most 8 chunks per lane.
+  const int kw = (!sol && SY_TUNE_STREAM_REREAD && (rc == 512 || rc == 1024)) ? (int)(rc / 256) : 1;
   int cpl = 1;
-  while (cpl * 32 < rc) cpl *= 2;
+  while (cpl * 32 * kw < rc) cpl *= 2;
   if (cpl > 8) return p;
   StreamCfg c{};
   c.BT = BT;
@@ -247,23 +250,26 @@ StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInf
   c.D = (int)D;
   c.row_chunks = (int)rc;
   c.row_bytes = (int)(D * es);
+  c.kw = kw;
   c.reread = (SY_TUNE_STREAM_REREAD && cpl == 8 && !sol) ? 1 : 0;
   c.warps = stream_threads(cpl, c.reread != 0) / 32;
   if (c.reread) {
-    // Whole tokens per warp, as even as possible: with t tokens per CTA and
-    // at most M warps, k = ceil(t / M) tokens per warp and ceil(t / k) warps,
-    // so no warp has more tokens than necessary (4096 tokens on 148 SMs:
-    // 14 warps x 2).
+    // Whole tokens per token stream (a warp, or K warps), as even as possible:
+    // with t tokens per CTA and at most M streams, k = ceil(t / M) tokens per
+    // stream and ceil(t / k) streams, so no stream has more tokens than
+    // necessary (4096 tokens on 148 SMs: 14 single-warp streams x 2).
     const int64_t g0 = BT < di.sms ? BT : di.sms;
     const int64_t t = (BT + g0 - 1) / g0;
-    const int64_t mw = kStreamRereadThreads / 32;
+    const int64_t mw = kStreamRereadThreads / 32 / kw;
     const int64_t k = (t + mw - 1) / mw;
-    c.warps = (int)((t + k - 1) / k);
+    c.warps = (int)((t + k - 1) / k) * kw;
+    if (k * N >= (int64_t)INT_MAX) return p;  // rows per stream are counted in 32 bits
   }
   c.stats_stride = (int)stats_stride(N);
   c.ring = 0;
   const int64_t fixed = (int64_t)stream_smem_layout(c).total;
-  int64_t ring = (di.max_smem - fixed) / ((int64_t)c.warps * (c.row_bytes + 8));
+  const int64_t per_row = (int64_t)(c.warps / kw) * (c.row_bytes + 8 + (kw > 1 ? 4 : 0));
+  int64_t ring = (di.max_smem - fixed - 16) / per_row;
   if (ring > 8) ring = 8;
   if (ring < 2) return p;
   c.ring = (int)ring;
@@ -593,11 +599,12 @@ int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype,
     const bool reg_first = top == kOpFwd && !sp.c.reread &&
                            plan_tile(kOpFwd, N, bt, D, dtype, di).kind == kPlanRegTile;
     if (sp.ok && !reg_first) {
+      const int kw = sp.c.kw > 1 ? sp.c.kw : 1;
       out[0] = kPlanStream;
       out[1] = sp.grid;
       out[2] = sp.c.ring;
-      out[3] = sp.c.warps;
-      out[4] = 32;
+      out[3] = sp.c.warps / kw;  // token streams per CTA
+      out[4] = 32 * kw;          // threads per token stream
       out[5] = sp.cpl;
       out[6] = sp.c.row_bytes;
       out[7] = sp.smem;

@@ -37,22 +37,29 @@ struct StreamCfg {
   int row_chunks;    // 16-byte chunks per row
   int row_bytes;     // padded to a multiple of 16 (rows are contiguous in HBM)
   int warps;         // W per CTA
-  int ring;          // R row buffers per warp
+  int ring;          // R row buffers per token stream (per warp, or per warp group)
   int stats_stride;
   int reread;        // 1: second pass reads the row again from shared memory
+  int kw;            // warps sharing one token (re-read variant; 0 or 1: one)
   float eps;
 };
 
 struct StreamSmem {
-  size_t w_off, ring_off, bar_off, zero_off, total;
+  size_t w_off, ring_off, bar_off, xch_off, cnt_off, zero_off, total;
 };
 
+// fp32 w, then the rings of the W / kw token streams, their full barriers, and
+// (kw > 1) the per-row exchange of partial sums and the buffer-release counters.
 __host__ __device__ inline StreamSmem stream_smem_layout(const StreamCfg& c) {
+  const int kw = c.kw > 1 ? c.kw : 1;
+  const size_t streams = (size_t)(c.warps / kw);
   StreamSmem s;
   s.w_off = 0;                                                   // fp32 w[D]
-  s.ring_off = ((size_t)c.D * 4 + 127) / 128 * 128;              // W * R rows
-  s.bar_off = s.ring_off + (size_t)c.warps * c.ring * c.row_bytes;
-  s.zero_off = s.bar_off + (size_t)c.warps * c.ring * 8;
+  s.ring_off = ((size_t)c.D * 4 + 127) / 128 * 128;              // streams * R rows
+  s.bar_off = s.ring_off + streams * c.ring * c.row_bytes;
+  s.xch_off = s.bar_off + streams * c.ring * 8;                  // float2 [streams][2][kw]
+  s.cnt_off = s.xch_off + (kw > 1 ? streams * 2 * kw * 8 : 0);   // int [streams][R]
+  s.zero_off = s.cnt_off + (kw > 1 ? (streams * c.ring * 4 + 15) / 16 * 16 : 0);
   s.total = s.zero_off + 16;
   return s;
 }
@@ -444,6 +451,195 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
   }
 }
 
+// Split variant of the re-read row stream for rows of K * 4 KiB (K = 2, 4: D =
+// 4096 / 8192 bf16): K warps share each token, warp k taking chunks
+// 256k .. 256k+255 of every row (8 per lane). Per row each warp reduces its
+// part of (dot, ssq) over its lanes; lane 0 publishes the pair, the K warps
+// meet at a named barrier and every warp adds the K pairs in warp order, so all
+// of them hold the bitwise-same logit, softmax state and weight. The row buffer
+// is shared: each warp, after its second pass over its part, adds one to the
+// buffer's counter and the warp that completes the count refills it (with the
+// group's row a ring-length ahead) -- no second barrier per row.
+template <typename T, int K>
+__global__ void __launch_bounds__(kStreamRereadThreads, 1)
+    stream_fwd_split_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
+                            T* __restrict__ out, float* __restrict__ stats, const StreamCfg c) {
+  constexpr int CPL = 8;
+  constexpr int VEC = Dt<T>::kVec;
+  constexpr int P = VEC / 2;
+  constexpr int RC = 256 * K;  // chunks per row
+  constexpr int RB = 16 * RC;  // bytes per row
+  const StreamSmem L = stream_smem_layout(c);
+  float* wsm = reinterpret_cast<float*>(sy_smem + L.w_off);
+  unsigned char* ring0 = sy_smem + L.ring_off;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sy_smem + L.bar_off);
+  float2* xch0 = reinterpret_cast<float2*>(sy_smem + L.xch_off);
+  int* cnt0 = reinterpret_cast<int*>(sy_smem + L.cnt_off);
+
+  const int tid = threadIdx.x;
+  const int lane = tid & 31;
+  const int wi = tid >> 5;
+  const int streams = c.warps / K;
+  if (c.kw != K || c.warps % K != 0 || c.warps != (int)(blockDim.x >> 5) || c.ring < 1 ||
+      !c.reread || c.row_chunks != RC || c.row_bytes != RB) {
+    if (tid == 0) record_device_error(kDevErrBadPlan);
+    return;
+  }
+  if (tid == 0) {
+    for (int i = 0; i < streams * c.ring; ++i) mbar_init(&bars[i], 1);
+    mbar_fence_init();
+  }
+  for (int i = tid; i < streams * c.ring; i += blockDim.x) cnt0[i] = 0;
+  for (int d = tid; d < c.D; d += blockDim.x) {
+    const int ch = d / VEC, e = d - ch * VEC;
+    wsm[((e >> 2) * RC + ch) * 4 + (e & 3)] = load_any(w, w_dtype, d);
+  }
+  __syncthreads();
+
+  const int gi = wi / K, wk = wi - gi * K;
+  const long long tstride = (long long)gridDim.x * streams;
+  const long long tok0 = blockIdx.x + (long long)gridDim.x * gi;
+  const int ntok = tok0 < c.BT ? (int)((c.BT - 1 - tok0) / tstride) + 1 : 0;
+  const int nrows = ntok * c.N;  // the planner keeps this below 2^31
+  unsigned char* ring = ring0 + (size_t)gi * c.ring * RB;
+  uint64_t* bar = bars + gi * c.ring;
+  float2* xch = xch0 + gi * 2 * K;
+  int* cnt = cnt0 + gi * c.ring;
+  const size_t nstride = (size_t)c.BT * RB;
+  // row q of this stream: source q mod N of token q / N
+  auto issue_row = [&](int slot_, int q) {
+    if (q >= nrows) return;
+    const int jj = q / c.N, nn = q - jj * c.N;
+    const unsigned char* src = reinterpret_cast<const unsigned char*>(v) + (size_t)nn * nstride +
+                               (size_t)(tok0 + tstride * jj) * RB;
+    mbar_arrive_expect_tx(&bar[slot_], (uint32_t)RB);
+    bulk_g2s(ring + (size_t)slot_ * RB, src, (uint32_t)RB, &bar[slot_], policy_evict_first());
+  };
+  if (wk == 0 && lane == 0)
+    for (int s = 0; s < c.ring; ++s) issue_row(s, s);
+
+  const int cb = wk * 256 + lane;  // this lane's chunks: cb + 32k
+  const float inv_d = 1.f / (float)c.D;
+  int q = 0;
+  for (int j = 0; j < ntok; ++j) {
+    float2 o[CPL][P];
+#pragma unroll
+    for (int k = 0; k < CPL; ++k)
+#pragma unroll
+      for (int i = 0; i < P; ++i) o[k][i] = make_float2(0.f, 0.f);
+    float mref = 0.f, mx = 0.f, l = 0.f;
+    float lane_logit = 0.f, lane_r = 0.f;  // row `lane`'s statistics (warp 0 of the stream)
+    float* st = stats != nullptr ? stats + (tok0 + tstride * j) * c.stats_stride : nullptr;
+    for (int n = 0; n < c.N; ++n, ++q) {
+      const int slot = q % c.ring;
+      if (!mbar_wait(&bar[slot], (uint32_t)((q / c.ring) & 1))) return;
+      const unsigned char* row = ring + (size_t)slot * RB;
+      // pass 1: this warp's part of dot and sum of squares
+      float2 dacc[2], sacc[2];
+#pragma unroll
+      for (int a = 0; a < 2; ++a) dacc[a] = sacc[a] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int k = 0; k < CPL; ++k) {
+        if (k % 4 == 0 && k > 0) __syncwarp();  // bounds the loads hoisted ahead (registers)
+        float2 x[P];
+        unpack2<T>(lds128(row + (cb + 32 * k) * 16), x);
+        const float4* wp = reinterpret_cast<const float4*>(wsm) + (cb + 32 * k);
+#pragma unroll
+        for (int i = 0; i < P; i += 2) {
+          const float4 wv = wp[(i / 2) * RC];
+          dacc[0] = __ffma2_rn(make_float2(wv.x, wv.y), x[i], dacc[0]);
+          sacc[0] = __ffma2_rn(x[i], x[i], sacc[0]);
+          dacc[1] = __ffma2_rn(make_float2(wv.z, wv.w), x[i + 1], dacc[1]);
+          sacc[1] = __ffma2_rn(x[i + 1], x[i + 1], sacc[1]);
+        }
+      }
+      dacc[0] = __fadd2_rn(dacc[0], dacc[1]);
+      sacc[0] = __fadd2_rn(sacc[0], sacc[1]);
+      float2 ds = make_float2(dacc[0].x + dacc[0].y, sacc[0].x + sacc[0].y);
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+        ds = __fadd2_rn(ds, make_float2(__shfl_xor_sync(kFull, ds.x, off),
+                                        __shfl_xor_sync(kFull, ds.y, off)));
+      // the K warps' parts, added in warp order by every warp
+      float2* xr = xch + (q & 1) * K;
+      if (lane == 0) xr[wk] = ds;
+      named_sync(1 + gi, 32 * K);
+      ds = xr[0];
+#pragma unroll
+      for (int k2 = 1; k2 < K; ++k2) ds = __fadd2_rn(ds, xr[k2]);
+      const float r = rsqrtf(ds.y * inv_d + c.eps);
+      const float logit = ds.x * r;
+      if (lane == (n & 31)) {
+        lane_logit = logit;
+        lane_r = r;
+      }
+      if (n >= 32 && st != nullptr && wk == 0 && lane == 0) {
+        st[n] = logit;
+        st[c.N + n] = r;
+      }
+      constexpr float kRescaleGap = 8.f;
+      float wgt = 1.f;
+      if (n == 0) {
+        mref = mx = logit;
+        l = 1.f;
+      } else {
+        mx = fmaxf(mx, logit);
+        if (logit > mref + kRescaleGap) {
+          const float sc = expf(mref - logit);
+          mref = logit;
+          l = fmaf(l, sc, 1.f);
+#pragma unroll
+          for (int k = 0; k < CPL; ++k)
+#pragma unroll
+            for (int i = 0; i < P; ++i) o[k][i] = __fmul2_rn(o[k][i], f2(sc));
+        } else {
+          wgt = expf(logit - mref);
+          l += wgt;
+        }
+      }
+      // pass 2: this warp's part of the row again, into o
+#pragma unroll
+      for (int k = 0; k < CPL; ++k) {
+        if (k % 4 == 0 && k > 0) __syncwarp();
+        float2 x[P];
+        unpack2<T>(lds128(row + (cb + 32 * k) * 16), x);
+#pragma unroll
+        for (int i = 0; i < P; ++i) o[k][i] = __ffma2_rn(f2(wgt), x[i], o[k][i]);
+      }
+      // release: the last of the K warps to finish with the buffer refills it
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence_block();
+        if (atomicAdd(&cnt[slot], 1) == K - 1) {
+          cnt[slot] = 0;
+          __threadfence_block();
+          fence_proxy_async();
+          issue_row(slot, q + c.ring);
+        }
+      }
+    }
+    const long long tok = tok0 + tstride * j;
+    if (st != nullptr && wk == 0) {
+      if (lane < c.N) {
+        st[lane] = lane_logit;
+        st[c.N + lane] = lane_r;
+      }
+      if (lane == 0) {
+        st[2 * c.N] = mx;
+        st[2 * c.N + 1] = mref + logf(l);
+      }
+    }
+    const float inv = 1.f / l;
+    T* orow = out + tok * c.D;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) {
+#pragma unroll
+      for (int i = 0; i < P; ++i) o[k][i] = __fmul2_rn(o[k][i], f2(inv));
+      stg128(orow + (cb + 32 * k) * VEC, pack2<T>(o[k]));
+    }
+  }
+}
+
 cudaError_t launch_stream_fwd(const StreamCfg& c, int grid, int cpl, int dtype, const void* v,
                               const void* w, int w_dtype, void* out, float* stats, bool sol,
                               cudaStream_t st);
@@ -457,9 +653,19 @@ cudaError_t launch_stream_tf(const StreamCfg& c, int grid, int cpl, const void* 
   T* op = static_cast<T*>(out);
   if (c.reread) {
     if constexpr (!SOL) {
-      if (cpl == 8 && (int)block.x <= kStreamRereadThreads)
-        return launch_smem(stream_fwd_reread_kernel<T, FULL>, grid, block, smem, st, vp, w,
-                           w_dtype, op, stats, c);
+      if (cpl == 8 && (int)block.x <= kStreamRereadThreads) {
+        if (c.kw <= 1)
+          return launch_smem(stream_fwd_reread_kernel<T, FULL>, grid, block, smem, st, vp, w,
+                             w_dtype, op, stats, c);
+        if constexpr (FULL) {
+          if (c.kw == 2)
+            return launch_smem(stream_fwd_split_kernel<T, 2>, grid, block, smem, st, vp, w,
+                               w_dtype, op, stats, c);
+          if (c.kw == 4)
+            return launch_smem(stream_fwd_split_kernel<T, 4>, grid, block, smem, st, vp, w,
+                               w_dtype, op, stats, c);
+        }
+      }
     }
     return cudaErrorInvalidValue;
   }
@@ -484,7 +690,7 @@ cudaError_t launch_stream_tf(const StreamCfg& c, int grid, int cpl, const void* 
 template <typename T, bool SOL>
 cudaError_t launch_stream_t(const StreamCfg& c, int grid, int cpl, const void* v, const void* w,
                             int w_dtype, void* out, float* stats, cudaStream_t st) {
-  if (c.row_chunks == 32 * cpl)
+  if (c.row_chunks == 32 * cpl * (c.kw > 1 ? c.kw : 1))
     return launch_stream_tf<T, SOL, true>(c, grid, cpl, v, w, w_dtype, out, stats, st);
   return launch_stream_tf<T, SOL, false>(c, grid, cpl, v, w, w_dtype, out, stats, st);
 }

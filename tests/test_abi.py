@@ -126,10 +126,10 @@ def test_planner_invariants_for_b200(native, dtype_name):
                     assert n <= 64
                 if p["kind"] == 1:
                     assert n <= 16
-                if p["kind"] == 3:  # row stream: forward only, 32 lanes x chunks >= row
-                    assert op == 0 and p["threads_per_group"] == 32
-                    assert p["chunks_per_thread"] * 32 * 16 >= d * dt.itemsize
-                    assert p["groups"] * 32 <= 512 and p["stages"] >= 2
+                if p["kind"] == 3:  # row stream: forward only, one token per 1, 2 or 4 warps
+                    assert op == 0 and p["threads_per_group"] in (32, 64, 128)
+                    assert p["chunks_per_thread"] * p["threads_per_group"] * 16 >= d * dt.itemsize
+                    assert p["groups"] * p["threads_per_group"] <= 512 and p["stages"] >= 2
     # representative forward: re-read row stream, 14 warps x 2 whole tokens each
     # (28 tokens per SM), at least 3 row buffers per warp
     rep = native.plan_info(0, 9, 4096, 2048, 1, torch.bfloat16, **B200)
@@ -137,6 +137,10 @@ def test_planner_invariants_for_b200(native, dtype_name):
     assert rep["grid"] * rep["groups"] * 2 >= 4096
     assert native.plan_info(0, 17, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 3
     assert native.plan_info(0, 9, 4096, 512, 1, torch.bfloat16, **B200)["kind"] == 1
+    # 8 and 16 KiB rows: the split row stream, 2 and 4 warps per token
+    for d, kw in ((4096, 2), (8192, 4)):
+        p = native.plan_info(0, 9, 4096, d, 1, torch.bfloat16, **B200)
+        assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw and p["stages"] >= 3
     assert native.plan_info(1, 9, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 1
     # rows that are not a multiple of 16 bytes go to the generic kernels
     assert native.plan_info(0, 3, 64, 777, 1, torch.bfloat16, **B200)["kind"] == 0

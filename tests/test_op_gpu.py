@@ -183,7 +183,8 @@ EPS_SHAPES = [  # fp32 shapes that reach every kernel family
     ((7, 2, 16, 512), PLAN_TILE, PLAN_TILE),
     ((9, 1, 48, 256), PLAN_TILE, PLAN_TILE),
     ((17, 1, 40, 1024), PLAN_STREAM, PLAN_SMEM_TILE),
-    ((10, 1, 24, 2048), PLAN_SMEM_TILE, PLAN_SMEM_TILE),
+    ((10, 1, 24, 2048), PLAN_STREAM, PLAN_SMEM_TILE),  # 8 KiB rows: split row stream
+    ((10, 1, 24, 1536), PLAN_SMEM_TILE, PLAN_SMEM_TILE),
     ((3, 1, 16, 777), PLAN_GENERIC, PLAN_GENERIC),
 ]
 
