@@ -10,6 +10,7 @@
 #include "sy_batched.cuh"
 #include "sy_reg.cuh"
 #include "sy_stream.cuh"
+#include "sy_stream_bwd.cuh"
 #include "sy_tile.cuh"
 
 // Planner tuning knobs. The defaults are the shipped configuration; builds
@@ -28,6 +29,9 @@
 #endif
 #ifndef SY_TUNE_STREAM_REREAD
 #define SY_TUNE_STREAM_REREAD 1  // forward, 8 chunks per lane: re-read row stream first
+#endif
+#ifndef SY_TUNE_STREAM_BWD
+#define SY_TUNE_STREAM_BWD 1  // backward: row stream before the shared-memory tile
 #endif
 
 namespace sy {
@@ -284,6 +288,58 @@ StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInf
   return p;
 }
 
+struct StreamBwdPlan {
+  bool ok = false;
+  StreamBwdCfg c{};
+  int grid = 0;
+  int64_t smem = 0;
+};
+
+// Row-stream backward: rows of exactly 128 * K chunks, K = 2 .. 16 warps per
+// token (4 .. 32 KiB rows at 2 bytes per element), N <= 32. Whole tokens per
+// token stream, as evenly as possible (as the forward's re-read stream).
+StreamBwdPlan plan_stream_bwd(int64_t N, int64_t BT, int64_t D, int dtype, const DevInfo& di) {
+  StreamBwdPlan p;
+  const int es = esize_of(dtype);
+  if (!SY_TUNE_STREAM_BWD || !es || N < 1 || N > kStreamBwdMaxN || D < 1 || D > kMaxD ||
+      BT < 1 || BT > INT_MAX)
+    return p;
+  if ((D * es) % 16) return p;
+  const int64_t rc = D * es / 16;
+  const int64_t per_warp = 32 * kStreamBwdCpl;
+  if (rc % per_warp) return p;
+  const int64_t kw = rc / per_warp;
+  if (kw < 2 || kw > 16) return p;
+  const int64_t max_streams = kStreamBwdThreads / 32 / kw;
+  const int64_t g0 = BT < di.sms ? BT : di.sms;
+  const int64_t t = (BT + g0 - 1) / g0;                // tokens per CTA
+  const int64_t k = (t + max_streams - 1) / max_streams;  // tokens per stream
+  const int64_t streams = (t + k - 1) / k;
+  if (k * (2 * N + 1) >= (int64_t)INT_MAX) return p;  // stream rows are counted in 32 bits
+  StreamBwdCfg c{};
+  c.BT = BT;
+  c.N = (int)N;
+  c.D = (int)D;
+  c.row_chunks = (int)rc;
+  c.row_bytes = (int)(D * es);
+  c.kw = (int)kw;
+  c.warps = (int)(streams * kw);
+  c.stats_stride = (int)stats_stride(N);
+  c.ring = 0;
+  const int64_t fixed = (int64_t)stream_bwd_smem_layout(c).total;
+  const int64_t per_row = streams * ((int64_t)c.row_bytes + 8 + 4);
+  int64_t ring = (di.max_smem - fixed - 16) / per_row;
+  if (ring > 8) ring = 8;
+  if (ring < 2) return p;
+  c.ring = (int)ring;
+  p.smem = (int64_t)stream_bwd_smem_layout(c).total;
+  if (p.smem > di.max_smem) return p;
+  p.c = c;
+  p.grid = (int)g0;
+  p.ok = true;
+  return p;
+}
+
 // Batched-query register tile: the fp32 tile (N * CPT * VEC floats per thread)
 // must fit kBatchedTileFloats; as many chunks per thread as fit (fewer warps
 // per token: less reduction work per query), groups of up to 256 threads, the
@@ -480,8 +536,11 @@ int64_t sy_bwd_partials(int64_t N, int64_t BT, int64_t D, int dtype) {
   DevInfo di;
   if (dev_info(&di) != cudaSuccess) return -SY_ERR_CUDA;
   const TilePlan p = plan_tile(kOpBwd, N, BT, D, dtype, di);
-  // register tile: one row per CTA; shared-memory tile: one row per group
+  // register tile and row stream: one row per CTA; shared-memory tile: one
+  // row per group
   if (p.kind == kPlanRegTile) return (int64_t)p.grid;
+  const StreamBwdPlan sb = plan_stream_bwd(N, BT, D, dtype, di);
+  if (sb.ok) return (int64_t)sb.grid;
   if (p.kind != kPlanGeneric) return (int64_t)p.grid * p.c.groups;
   return generic_partials(BT, di);
 }
@@ -504,10 +563,21 @@ int sy_bwd(const void* v, const void* w, const void* g, const float* stats, void
   DevInfo di;
   cudaError_t e = dev_info(&di);
   if (e != cudaSuccess) return cuda_status(e, "sy_bwd: device query");
+  // Order: the register tile (N <= 16, rows up to 4 KiB), the row stream
+  // (rows of 128 * K chunks, N <= 32), the shared-memory tile, generic.
   TilePlan p = plan_tile(kOpBwd, N, BT, D, dtype, di);
   p.c.eps = eps;
-  if (p.kind != kPlanGeneric && al16(v) && al16(g) && al16(stats) && al16(dv) &&
-      al16(dw_partial)) {
+  const bool aligned = al16(v) && al16(g) && al16(stats) && al16(dv) && al16(dw_partial);
+  if (p.kind == kPlanRegTile && aligned) {
+    e = launch_plan_bwd(p, dtype, v, w, w_dtype, g, stats, dv, dw_partial, st);
+    return cuda_status(e, "sy_bwd: register-tile kernel launch");
+  }
+  const StreamBwdPlan sb = plan_stream_bwd(N, BT, D, dtype, di);
+  if (sb.ok && aligned) {
+    e = launch_stream_bwd(sb.c, sb.grid, dtype, v, w, w_dtype, g, stats, dv, dw_partial, st);
+    return cuda_status(e, "sy_bwd: stream kernel launch");
+  }
+  if (p.kind != kPlanGeneric && aligned) {
     e = launch_plan_bwd(p, dtype, v, w, w_dtype, g, stats, dv, dw_partial, st);
     return cuda_status(e, "sy_bwd: tile kernel launch");
   }
@@ -608,6 +678,20 @@ int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype,
       out[5] = sp.cpl;
       out[6] = sp.c.row_bytes;
       out[7] = sp.smem;
+      return SY_OK;
+    }
+  }
+  if (top == kOpBwd && plan_tile(kOpBwd, N, bt, D, dtype, di).kind != kPlanRegTile) {
+    const StreamBwdPlan sb = plan_stream_bwd(N, bt, D, dtype, di);
+    if (sb.ok) {
+      out[0] = kPlanStream;
+      out[1] = sb.grid;
+      out[2] = sb.c.ring;
+      out[3] = sb.c.warps / sb.c.kw;  // token streams per CTA
+      out[4] = 32 * sb.c.kw;          // threads per token stream
+      out[5] = kStreamBwdCpl;
+      out[6] = sb.c.row_bytes;
+      out[7] = sb.smem;
       return SY_OK;
     }
   }

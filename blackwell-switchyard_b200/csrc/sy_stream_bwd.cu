@@ -1,0 +1,33 @@
+// sy_stream_bwd.cu -- instantiations and launcher of the row-stream backward.
+#include "sy_stream_bwd.cuh"
+
+namespace sy {
+
+template <typename T>
+static cudaError_t launch_stream_bwd_t(const StreamBwdCfg& c, int grid, const void* v,
+                                       const void* w, int w_dtype, const void* g,
+                                       const float* stats, void* dv, float* dw_partial,
+                                       cudaStream_t st) {
+  if (c.warps * 32 > kStreamBwdThreads) return cudaErrorInvalidConfiguration;
+  return launch_smem(stream_bwd_kernel<T>, grid, dim3(c.warps * 32),
+                     stream_bwd_smem_layout(c).total, st, static_cast<const T*>(v), w, w_dtype,
+                     static_cast<const T*>(g), stats, static_cast<T*>(dv), dw_partial, c);
+}
+
+cudaError_t launch_stream_bwd(const StreamBwdCfg& c, int grid, int dtype, const void* v,
+                              const void* w, int w_dtype, const void* g, const float* stats,
+                              void* dv, float* dw_partial, cudaStream_t st) {
+  switch (dtype) {
+    case SY_BF16:
+      return launch_stream_bwd_t<__nv_bfloat16>(c, grid, v, w, w_dtype, g, stats, dv, dw_partial,
+                                                st);
+    case SY_F16:
+      return launch_stream_bwd_t<__half>(c, grid, v, w, w_dtype, g, stats, dv, dw_partial, st);
+    case SY_F32:
+      return launch_stream_bwd_t<float>(c, grid, v, w, w_dtype, g, stats, dv, dw_partial, st);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace sy

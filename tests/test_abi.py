@@ -126,10 +126,15 @@ def test_planner_invariants_for_b200(native, dtype_name):
                     assert n <= 64
                 if p["kind"] == 1:
                     assert n <= 16
-                if p["kind"] == 3:  # row stream: forward only, one token per 1, 2 or 4 warps
-                    assert op == 0 and p["threads_per_group"] in (32, 64, 128)
+                if p["kind"] == 3 and op == 0:  # row-stream forward: a token per 1, 2 or 4 warps
+                    assert p["threads_per_group"] in (32, 64, 128)
                     assert p["chunks_per_thread"] * p["threads_per_group"] * 16 >= d * dt.itemsize
                     assert p["groups"] * p["threads_per_group"] <= 512 and p["stages"] >= 2
+                if p["kind"] == 3 and op == 1:  # row-stream backward: 4 chunks per lane, exact
+                    assert 2 <= p["threads_per_group"] // 32 <= 16 and n <= 32
+                    assert p["chunks_per_thread"] * p["threads_per_group"] * 16 == d * dt.itemsize
+                    assert p["groups"] * p["threads_per_group"] <= 512 and p["stages"] >= 2
+                    assert p["groups"] <= 8  # named barrier ids 1..8
     # representative forward: re-read row stream, 14 warps x 2 whole tokens each
     # (28 tokens per SM), at least 3 row buffers per warp
     rep = native.plan_info(0, 9, 4096, 2048, 1, torch.bfloat16, **B200)
@@ -142,5 +147,9 @@ def test_planner_invariants_for_b200(native, dtype_name):
         p = native.plan_info(0, 9, 4096, d, 1, torch.bfloat16, **B200)
         assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw and p["stages"] >= 3
     assert native.plan_info(1, 9, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 1
+    # backward rows the register tile cannot hold: the row stream, K = rows / 2 KiB
+    for n, d, kw in ((9, 8192, 8), (17, 4096, 4), (17, 2048, 2)):
+        p = native.plan_info(1, n, 4096, d, 1, torch.bfloat16, **B200)
+        assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw and p["stages"] >= 3
     # rows that are not a multiple of 16 bytes go to the generic kernels
     assert native.plan_info(0, 3, 64, 777, 1, torch.bfloat16, **B200)["kind"] == 0

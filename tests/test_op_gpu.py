@@ -165,6 +165,10 @@ def test_dispatch_sends_the_representative_shape_to_the_tile_kernels():
     assert _plan("fwd", 9, 4096, 512, torch.bfloat16) == PLAN_TILE
     # more sources than the register tile holds: the row-stream forward
     assert _plan("fwd", 17, 4096, 2048, torch.bfloat16) == PLAN_STREAM
+    # rows or source counts the register-tile backward cannot hold: the
+    # row-stream backward (K warps per token, rows read twice)
+    for n, d in ((9, 8192), (17, 4096), (17, 2048), (32, 4096)):
+        assert _plan("bwd", n, 4096, d, torch.bfloat16) == PLAN_STREAM
     # batched queries: the register tile reused across queries; tiles that do
     # not fit registers (N=17, D=4096) take the generic kernel
     for s in (2, 4, 8, 16):
@@ -182,9 +186,10 @@ EPS_SHAPES = [  # fp32 shapes that reach every kernel family
     ((9, 1, 64, 1024), PLAN_STREAM, PLAN_TILE),  # 4 KiB rows: re-read row stream
     ((7, 2, 16, 512), PLAN_TILE, PLAN_TILE),
     ((9, 1, 48, 256), PLAN_TILE, PLAN_TILE),
-    ((17, 1, 40, 1024), PLAN_STREAM, PLAN_SMEM_TILE),
-    ((10, 1, 24, 2048), PLAN_STREAM, PLAN_SMEM_TILE),  # 8 KiB rows: split row stream
-    ((10, 1, 24, 1536), PLAN_SMEM_TILE, PLAN_SMEM_TILE),
+    ((17, 1, 40, 1024), PLAN_STREAM, PLAN_STREAM),  # backward: 2 warps per token
+    ((10, 1, 24, 2048), PLAN_STREAM, PLAN_STREAM),  # 8 KiB rows: split row streams
+    ((10, 1, 24, 1536), PLAN_SMEM_TILE, PLAN_STREAM),  # backward: 3 warps per token
+    ((33, 1, 24, 512), PLAN_STREAM, PLAN_SMEM_TILE),
     ((3, 1, 16, 777), PLAN_GENERIC, PLAN_GENERIC),
 ]
 
@@ -312,6 +317,35 @@ def test_representative_shape_full_size_properties():
     sol = speed_of_light(v)
     s_ref = O.speed_of_light(np64(v[:, :, toks]))
     assert O.rel_l2(np64(sol[:, toks]), s_ref) <= 1.005 * O.dtype_floor(s_ref, "bfloat16")
+
+
+@pytest.mark.parametrize("shape,dtype", [
+    ((9, 1, 1024, 8192), torch.bfloat16),   # 16 KiB rows: 8 warps per token, 4 tokens per stream
+    ((17, 1, 1024, 4096), torch.bfloat16),  # N > 16: 4 warps per token
+    ((24, 1, 1200, 2048), torch.float16),   # 2 warps per token, 6-7 rows in each ring
+])
+def test_row_stream_backward_many_tokens_per_stream(shape, dtype):
+    """The row-stream backward with several tokens per token stream (the ring
+    wraps many times, the G exchange alternates its two buffers): dv on a
+    sample of tokens against the oracle, dw against a chunked float64 sum over
+    every token, both at the dtype's rounding floor, and bitwise stable."""
+    n, b, t, d = shape
+    assert _plan("bwd", n, b * t, d, dtype) == PLAN_STREAM
+    name = {torch.bfloat16: "bfloat16", torch.float16: "float16"}[dtype]
+    v = randn(*shape, dtype=dtype, seed=3)
+    w = randn(d, dtype=dtype, seed=4, scale=d ** -0.5)
+    g = randn(b, t, d, dtype=dtype, seed=5)
+    out, dv, dw = fwd_bwd(v, w, g)
+    out2, dv2, dw2 = fwd_bwd(v, w, g)
+    assert torch.equal(out, out2) and torch.equal(dv, dv2) and torch.equal(dw, dw2)
+    toks = torch.randperm(t, generator=torch.Generator().manual_seed(6))[:64].sort().values
+    ww = np64(w)
+    dv_ref, _ = O.backward(np64(v[:, :, toks]), ww, np64(g[:, toks]))
+    assert O.rel_l2(np64(dv[:, :, toks]), dv_ref) <= 1.005 * O.dtype_floor(dv_ref, name)
+    dw_ref = np.zeros(d)
+    for c in range(0, t, 256):
+        dw_ref += O.backward(np64(v[:, :, c:c + 256]), ww, np64(g[:, c:c + 256]))[1]
+    assert O.rel_l2(np64(dw), dw_ref) <= 1.005 * O.dtype_floor(dw_ref, name)
 
 
 def test_backward_accumulates_dw_in_fp32():

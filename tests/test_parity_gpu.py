@@ -116,7 +116,8 @@ def test_backward_matches_oracle(shape):
 
 
 @pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
-@pytest.mark.parametrize("shape", [(4, 2, 128, 512), (9, 1, 64, 2048), (3, 1, 64, 777), (33, 1, 16, 512)])
+@pytest.mark.parametrize("shape", [(4, 2, 128, 512), (9, 1, 64, 2048), (3, 1, 64, 777), (33, 1, 16, 512),
+                                   (17, 1, 48, 4096)])
 def test_backward_other_dtypes(shape, dtype):
     v, w = make(*shape, dtype, seed=5)
     g = torch.randn(shape[1:], generator=torch.Generator().manual_seed(6)).to(dtype).to(DEV)
