@@ -273,6 +273,27 @@ __device__ __forceinline__ void unpack2(const uint4& u, float2* p) {
   for (int i = 0; i < Dt<T>::kVec / 2; ++i) p[i] = make_float2(x[2 * i], x[2 * i + 1]);
 }
 
+// Mixed-precision FMA on packed 16-bit pairs (sm_100: fma.rn.f32.{bf16,f16}):
+// acc.x += lo(a) * lo(b), acc.y += hi(a) * hi(b), one fp32 rounding each. The
+// 16-bit operands convert to fp32 exactly and their product is exact in fp32,
+// so this equals __ffma2_rn on the unpacked values -- without the unpacking.
+template <typename T>
+__device__ __forceinline__ void mixfma2(float2& acc, uint32_t a, uint32_t b);
+template <>
+__device__ __forceinline__ void mixfma2<__nv_bfloat16>(float2& acc, uint32_t a, uint32_t b) {
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %2;\n\tmov.b32 {bl, bh}, %3;\n\t"
+      "fma.rn.f32.bf16 %0, al, bl, %0;\n\tfma.rn.f32.bf16 %1, ah, bh, %1;\n\t}"
+      : "+f"(acc.x), "+f"(acc.y)
+      : "r"(a), "r"(b));
+}
+template <>
+__device__ __forceinline__ void mixfma2<__half>(float2& acc, uint32_t a, uint32_t b) {
+  asm("{\n\t.reg .b16 al, ah, bl, bh;\n\tmov.b32 {al, ah}, %2;\n\tmov.b32 {bl, bh}, %3;\n\t"
+      "fma.rn.f32.f16 %0, al, bl, %0;\n\tfma.rn.f32.f16 %1, ah, bh, %1;\n\t}"
+      : "+f"(acc.x), "+f"(acc.y)
+      : "r"(a), "r"(b));
+}
+
 template <typename T>
 __device__ __forceinline__ uint4 pack2(const float2* p) {
   float x[Dt<T>::kVec];

@@ -261,6 +261,29 @@ __global__ void __launch_bounds__(stream_threads(CPL), 1)
   }
 }
 
+// Stage w in shared memory for the re-read kernels. MIX: in its own 16-bit
+// type, row layout (chunk ch at byte 16 ch), copied in 16-byte chunks when w is
+// aligned; otherwise fp32 in VEC/4 planes of float4 per chunk (plane p of
+// chunk ch at float4 p * rc + ch), conflict-free for lane-consecutive chunks.
+template <typename T, bool MIX>
+__device__ __forceinline__ void stage_w(float* wsm, const void* w, int w_dtype, int D, int rc) {
+  constexpr int VEC = Dt<T>::kVec;
+  if constexpr (MIX) {
+    if ((reinterpret_cast<uintptr_t>(w) & 15u) == 0) {
+      for (int ch = threadIdx.x; ch < rc; ch += blockDim.x)
+        reinterpret_cast<uint4*>(wsm)[ch] = reinterpret_cast<const uint4*>(w)[ch];
+    } else {
+      for (int d = threadIdx.x; d < D; d += blockDim.x)
+        reinterpret_cast<T*>(wsm)[d] = reinterpret_cast<const T*>(w)[d];
+    }
+  } else {
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+      const int ch = d / VEC, e = d - ch * VEC;
+      wsm[((e >> 2) * rc + ch) * 4 + (e & 3)] = load_any(w, w_dtype, d);
+    }
+  }
+}
+
 // Re-read variant of the row stream (8 chunks per lane: 4 KiB rows). Per row,
 // pass 1 reads the lane's chunks from the row buffer for the dot and the sum
 // of squares only; after the online-softmax update pass 2 reads them again
@@ -270,7 +293,7 @@ __global__ void __launch_bounds__(stream_threads(CPL), 1)
 // counters and one running source pointer, so 14 warps (128 registers) fit
 // on an SM: with whole tokens per warp that balances 28 tokens per SM as
 // 2 per warp (the representative 4096 tokens on 148 SMs).
-template <typename T, bool FULL>
+template <typename T, bool FULL, bool MIX>
 __global__ void __launch_bounds__(kStreamRereadThreads, 1)
     stream_fwd_reread_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
                              T* __restrict__ out, float* __restrict__ stats, const StreamCfg c) {
@@ -297,10 +320,9 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
     *reinterpret_cast<uint4*>(sy_smem + L.zero_off) = make_uint4(0u, 0u, 0u, 0u);
     mbar_fence_init();
   }
-  for (int d = tid; d < c.D; d += blockDim.x) {
-    const int ch = d / VEC, e = d - ch * VEC;
-    wsm[((e >> 2) * c.row_chunks + ch) * 4 + (e & 3)] = load_any(w, w_dtype, d);
-  }
+  // w is staged before the rings start filling: issued after the bulk copies,
+  // its loads would wait behind them.
+  stage_w<T, MIX>(wsm, w, w_dtype, c.D, c.row_chunks);
   __syncthreads();
 
   // This warp's tokens: tok0 + tstride * j, j < ntok (fewer than 2^31 rows
@@ -356,16 +378,33 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
 #pragma unroll
       for (int k = 0; k < CPL; ++k) {
         if (k % 4 == 0 && k > 0) __syncwarp();  // bounds the loads hoisted ahead (registers)
-        float2 x[P];
-        unpack2<T>(lds128(cval(k) ? row + (lane + 32 * k) * 16 : zero_pad), x);
-        const float4* wp = reinterpret_cast<const float4*>(wsm) + (lane + 32 * k);
+        if constexpr (MIX) {
+          // the same products and accumulation order as below, on the packed
+          // 16-bit halves (pair i of the chunk is word i)
+          const uint4 xu = lds128(cval(k) ? row + (lane + 32 * k) * 16 : zero_pad);
+          const uint4 wu = lds128(cval(k) ? reinterpret_cast<const unsigned char*>(wsm) +
+                                                (lane + 32 * k) * 16
+                                          : zero_pad);
+          mixfma2<T>(dacc[0], wu.x, xu.x);
+          mixfma2<T>(sacc[0], xu.x, xu.x);
+          mixfma2<T>(dacc[A - 1], wu.y, xu.y);
+          mixfma2<T>(sacc[A - 1], xu.y, xu.y);
+          mixfma2<T>(dacc[0], wu.z, xu.z);
+          mixfma2<T>(sacc[0], xu.z, xu.z);
+          mixfma2<T>(dacc[A - 1], wu.w, xu.w);
+          mixfma2<T>(sacc[A - 1], xu.w, xu.w);
+        } else {
+          float2 x[P];
+          unpack2<T>(lds128(cval(k) ? row + (lane + 32 * k) * 16 : zero_pad), x);
+          const float4* wp = reinterpret_cast<const float4*>(wsm) + (lane + 32 * k);
 #pragma unroll
-        for (int i = 0; i < P; i += 2) {
-          const float4 wv = cval(k) ? wp[(i / 2) * RC] : make_float4(0.f, 0.f, 0.f, 0.f);
-          dacc[0] = __ffma2_rn(make_float2(wv.x, wv.y), x[i], dacc[0]);
-          sacc[0] = __ffma2_rn(x[i], x[i], sacc[0]);
-          dacc[A - 1] = __ffma2_rn(make_float2(wv.z, wv.w), x[i + 1], dacc[A - 1]);
-          sacc[A - 1] = __ffma2_rn(x[i + 1], x[i + 1], sacc[A - 1]);
+          for (int i = 0; i < P; i += 2) {
+            const float4 wv = cval(k) ? wp[(i / 2) * RC] : make_float4(0.f, 0.f, 0.f, 0.f);
+            dacc[0] = __ffma2_rn(make_float2(wv.x, wv.y), x[i], dacc[0]);
+            sacc[0] = __ffma2_rn(x[i], x[i], sacc[0]);
+            dacc[A - 1] = __ffma2_rn(make_float2(wv.z, wv.w), x[i + 1], dacc[A - 1]);
+            sacc[A - 1] = __ffma2_rn(x[i + 1], x[i + 1], sacc[A - 1]);
+          }
         }
       }
 #pragma unroll
@@ -460,7 +499,7 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
 // is shared: each warp, after its second pass over its part, adds one to the
 // buffer's counter and the warp that completes the count refills it (with the
 // group's row a ring-length ahead) -- no second barrier per row.
-template <typename T, int K>
+template <typename T, int K, bool MIX>
 __global__ void __launch_bounds__(kStreamRereadThreads, 1)
     stream_fwd_split_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
                             T* __restrict__ out, float* __restrict__ stats, const StreamCfg c) {
@@ -490,10 +529,7 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
     mbar_fence_init();
   }
   for (int i = tid; i < streams * c.ring; i += blockDim.x) cnt0[i] = 0;
-  for (int d = tid; d < c.D; d += blockDim.x) {
-    const int ch = d / VEC, e = d - ch * VEC;
-    wsm[((e >> 2) * RC + ch) * 4 + (e & 3)] = load_any(w, w_dtype, d);
-  }
+  stage_w<T, MIX>(wsm, w, w_dtype, c.D, RC);
   __syncthreads();
 
   const int gi = wi / K, wk = wi - gi * K;
@@ -541,16 +577,29 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
 #pragma unroll
       for (int k = 0; k < CPL; ++k) {
         if (k % 4 == 0 && k > 0) __syncwarp();  // bounds the loads hoisted ahead (registers)
-        float2 x[P];
-        unpack2<T>(lds128(row + (cb + 32 * k) * 16), x);
-        const float4* wp = reinterpret_cast<const float4*>(wsm) + (cb + 32 * k);
+        if constexpr (MIX) {
+          const uint4 xu = lds128(row + (cb + 32 * k) * 16);
+          const uint4 wu = lds128(reinterpret_cast<const unsigned char*>(wsm) + (cb + 32 * k) * 16);
+          mixfma2<T>(dacc[0], wu.x, xu.x);
+          mixfma2<T>(sacc[0], xu.x, xu.x);
+          mixfma2<T>(dacc[1], wu.y, xu.y);
+          mixfma2<T>(sacc[1], xu.y, xu.y);
+          mixfma2<T>(dacc[0], wu.z, xu.z);
+          mixfma2<T>(sacc[0], xu.z, xu.z);
+          mixfma2<T>(dacc[1], wu.w, xu.w);
+          mixfma2<T>(sacc[1], xu.w, xu.w);
+        } else {
+          float2 x[P];
+          unpack2<T>(lds128(row + (cb + 32 * k) * 16), x);
+          const float4* wp = reinterpret_cast<const float4*>(wsm) + (cb + 32 * k);
 #pragma unroll
-        for (int i = 0; i < P; i += 2) {
-          const float4 wv = wp[(i / 2) * RC];
-          dacc[0] = __ffma2_rn(make_float2(wv.x, wv.y), x[i], dacc[0]);
-          sacc[0] = __ffma2_rn(x[i], x[i], sacc[0]);
-          dacc[1] = __ffma2_rn(make_float2(wv.z, wv.w), x[i + 1], dacc[1]);
-          sacc[1] = __ffma2_rn(x[i + 1], x[i + 1], sacc[1]);
+          for (int i = 0; i < P; i += 2) {
+            const float4 wv = wp[(i / 2) * RC];
+            dacc[0] = __ffma2_rn(make_float2(wv.x, wv.y), x[i], dacc[0]);
+            sacc[0] = __ffma2_rn(x[i], x[i], sacc[0]);
+            dacc[1] = __ffma2_rn(make_float2(wv.z, wv.w), x[i + 1], dacc[1]);
+            sacc[1] = __ffma2_rn(x[i + 1], x[i + 1], sacc[1]);
+          }
         }
       }
       dacc[0] = __fadd2_rn(dacc[0], dacc[1]);
@@ -644,6 +693,28 @@ cudaError_t launch_stream_fwd(const StreamCfg& c, int grid, int cpl, int dtype, 
                               const void* w, int w_dtype, void* out, float* stats, bool sol,
                               cudaStream_t st);
 
+#ifndef SY_TUNE_FWD_MIX
+#define SY_TUNE_FWD_MIX 1
+#endif
+
+template <typename T, bool FULL, bool MIX>
+cudaError_t launch_stream_reread(const StreamCfg& c, int grid, dim3 block, size_t smem,
+                                 const T* vp, const void* w, int w_dtype, T* op, float* stats,
+                                 cudaStream_t st) {
+  if (c.kw <= 1)
+    return launch_smem(stream_fwd_reread_kernel<T, FULL, MIX>, grid, block, smem, st, vp, w,
+                       w_dtype, op, stats, c);
+  if constexpr (FULL) {
+    if (c.kw == 2)
+      return launch_smem(stream_fwd_split_kernel<T, 2, MIX>, grid, block, smem, st, vp, w,
+                         w_dtype, op, stats, c);
+    if (c.kw == 4)
+      return launch_smem(stream_fwd_split_kernel<T, 4, MIX>, grid, block, smem, st, vp, w,
+                         w_dtype, op, stats, c);
+  }
+  return cudaErrorInvalidValue;
+}
+
 template <typename T, bool SOL, bool FULL>
 cudaError_t launch_stream_tf(const StreamCfg& c, int grid, int cpl, const void* v, const void* w,
                              int w_dtype, void* out, float* stats, cudaStream_t st) {
@@ -654,17 +725,14 @@ cudaError_t launch_stream_tf(const StreamCfg& c, int grid, int cpl, const void* 
   if (c.reread) {
     if constexpr (!SOL) {
       if (cpl == 8 && (int)block.x <= kStreamRereadThreads) {
-        if (c.kw <= 1)
-          return launch_smem(stream_fwd_reread_kernel<T, FULL>, grid, block, smem, st, vp, w,
-                             w_dtype, op, stats, c);
-        if constexpr (FULL) {
-          if (c.kw == 2)
-            return launch_smem(stream_fwd_split_kernel<T, 2>, grid, block, smem, st, vp, w,
-                               w_dtype, op, stats, c);
-          if (c.kw == 4)
-            return launch_smem(stream_fwd_split_kernel<T, 4>, grid, block, smem, st, vp, w,
-                               w_dtype, op, stats, c);
+        // w of the sources' own 16-bit type: pass 1 on the packed halves
+        if constexpr (sizeof(T) == 2) {
+          if (w_dtype == Dt<T>::kCode && SY_TUNE_FWD_MIX)
+            return launch_stream_reread<T, FULL, true>(c, grid, block, smem, vp, w, w_dtype, op,
+                                                       stats, st);
         }
+        return launch_stream_reread<T, FULL, false>(c, grid, block, smem, vp, w, w_dtype, op,
+                                                    stats, st);
       }
     }
     return cudaErrorInvalidValue;

@@ -319,6 +319,27 @@ def test_representative_shape_full_size_properties():
     assert O.rel_l2(np64(sol[:, toks]), s_ref) <= 1.005 * O.dtype_floor(s_ref, "bfloat16")
 
 
+@pytest.mark.parametrize("shape", [(9, 1, 600, 2048), (9, 1, 300, 4096), (9, 1, 150, 8192),
+                                   (4, 2, 100, 1800)])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_forward_same_bits_for_16bit_and_fp32_queries(shape, dtype):
+    """A query of the sources' own 16-bit type takes the packed mixed-precision
+    dot product (fma.rn.f32.{bf16,f16} on the 16-bit halves); the same values
+    as an fp32 query take the unpacked path. Products are exact and the
+    accumulation order is the same, so out and the statistics agree bitwise."""
+    n, b, t, d = shape
+    v = randn(*shape, dtype=dtype, seed=7)
+    w = randn(d, dtype=dtype, seed=8, scale=d ** -0.5)
+    out16 = block_attn_res_triton(v, w)
+    out32 = block_attn_res_triton(v, w.float())
+    assert torch.equal(out16, out32)
+    stats = [torch.empty(b * t, _native.stats_stride(n), device=DEV) for _ in range(2)]
+    o = [torch.empty(b, t, d, dtype=dtype, device=DEV) for _ in range(2)]
+    _native.fwd(v, w, o[0], stats[0], n, b * t, d, DEFAULT_EPS)
+    _native.fwd(v, w.float(), o[1], stats[1], n, b * t, d, DEFAULT_EPS)
+    assert torch.equal(o[0], o[1]) and torch.equal(stats[0], stats[1])
+
+
 @pytest.mark.parametrize("shape,dtype", [
     ((9, 1, 1024, 8192), torch.bfloat16),   # 16 KiB rows: 8 warps per token, 4 tokens per stream
     ((17, 1, 1024, 4096), torch.bfloat16),  # N > 16: 4 warps per token
