@@ -531,16 +531,30 @@ __global__ void __launch_bounds__(reg_threads(N, CPT, Dt<T>::kVec, true), 1)
     for (int i = 0; i < M; ++i) a[i] = 0.f;
 #pragma unroll
     for (int cc = 0; cc < CPT; ++cc) {
-      float2 gp[P];
-      unpack2<T>(gx[cc], gp);
+      if constexpr (sizeof(T) == 2) {
+        // packed 16-bit halves, word i = pair i: the same products and order
+        // as the unpacked form below, without unpacking the tile
 #pragma unroll
-      for (int n = 0; n < N; ++n) {
-        float2 p[P];
-        unpack2<T>(x[n][cc], p);
-        float2 acc = make_float2(0.f, 0.f);
+        for (int n = 0; n < N; ++n) {
+          float2 acc = make_float2(0.f, 0.f);
+          mixfma2<T>(acc, gx[cc].x, x[n][cc].x);
+          mixfma2<T>(acc, gx[cc].y, x[n][cc].y);
+          mixfma2<T>(acc, gx[cc].z, x[n][cc].z);
+          mixfma2<T>(acc, gx[cc].w, x[n][cc].w);
+          a[n] += acc.x + acc.y;
+        }
+      } else {
+        float2 gp[P];
+        unpack2<T>(gx[cc], gp);
 #pragma unroll
-        for (int i = 0; i < P; ++i) acc = __ffma2_rn(gp[i], p[i], acc);
-        a[n] += acc.x + acc.y;
+        for (int n = 0; n < N; ++n) {
+          float2 p[P];
+          unpack2<T>(x[n][cc], p);
+          float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int i = 0; i < P; ++i) acc = __ffma2_rn(gp[i], p[i], acc);
+          a[n] += acc.x + acc.y;
+        }
       }
     }
     const float tot_l = warp_reduce_scatter<M>(a, lane);
