@@ -69,6 +69,8 @@ def parse_args():
                     default=None,
                     help="no timing: run 5 launches of one kernel (or step) at the representative "
                          "shape, for an ncu capture; prints nothing")
+    ap.add_argument("--shape", default=None,
+                    help="N,B,T,D for --profile (default: the representative shape)")
     return ap.parse_args()
 
 
@@ -516,8 +518,18 @@ def kernel_label(native, op: str, n: int, bt: int, d: int) -> str:
     info = native.plan_info(code, n, bt, d, 1, torch.bfloat16)
     kind = info["kind"]
     if kind == 3:
-        name = "stream_fwd_reread_kernel" if info["chunks_per_thread"] == 8 else "stream_fwd_kernel"
-        shape = f"row stream, {info['groups']} warps x 1 token, {info['stages']} row buffers/warp"
+        streams = info["grid"] * info["groups"]
+        per = -(-bt // streams)  # whole tokens per token stream (at most)
+        kw = info["threads_per_group"] // 32
+        if op == "bwd":
+            name = "stream_bwd_kernel"
+        elif info["chunks_per_thread"] == 8:
+            name = "stream_fwd_reread_kernel" if kw == 1 else "stream_fwd_split_kernel"
+        else:
+            name = "stream_fwd_kernel"
+        who = "warps" if kw == 1 else f"streams of {kw} warps"
+        shape = (f"row stream, {info['groups']} {who} x {per} tokens, "
+                 f"{info['stages']} row buffers per stream")
     elif kind == 1:
         name = f"reg_{op}_kernel"
         shape = (f"register tile, {info['groups']} groups x {info['threads_per_group'] // 32} warps, "
@@ -594,14 +606,15 @@ def run_reference(args):
     }), flush=True)
 
 
-def run_profile(kind: str):
-    """A handful of launches at the representative shape and nothing else, so
-    that an ncu capture ends by itself in seconds."""
+def run_profile(kind: str, shape: str | None = None):
+    """A handful of launches at the representative shape (or `shape`,
+    "N,B,T,D") and nothing else, so that an ncu capture ends by itself in
+    seconds."""
     from switchyard import _native, block_attn_res_batched, block_attn_res_triton
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    n, b, t, d = REP
+    n, b, t, d = tuple(int(x) for x in shape.split(",")) if shape else REP
     v, w, dout = make_inputs(dev, 0, n, b, t, d)
     bt = b * t
     out = torch.empty(b, t, d, device=dev, dtype=v.dtype)
@@ -632,7 +645,7 @@ def main():
     faulthandler.enable()
     args = parse_args()
     if args.profile:
-        run_profile(args.profile)
+        run_profile(args.profile, args.shape)
         return
     if args.impl == "reference":
         run_reference(args)
