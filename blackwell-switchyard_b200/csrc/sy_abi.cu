@@ -10,6 +10,7 @@
 #include "sy_batched.cuh"
 #include "sy_reg.cuh"
 #include "sy_stream.cuh"
+#include "sy_stream_batched.cuh"
 #include "sy_stream_bwd.cuh"
 #include "sy_tile.cuh"
 
@@ -32,6 +33,9 @@
 #endif
 #ifndef SY_TUNE_STREAM_BWD
 #define SY_TUNE_STREAM_BWD 1  // backward: row stream before the shared-memory tile
+#endif
+#ifndef SY_TUNE_BATCHED_REG
+#define SY_TUNE_BATCHED_REG 1  // batched: the register tile where it fits (else row stream)
 #endif
 
 namespace sy {
@@ -346,6 +350,7 @@ StreamBwdPlan plan_stream_bwd(int64_t N, int64_t BT, int64_t D, int dtype, const
 // queries' S rows in shared memory beside the ring.
 TilePlan plan_batched(int64_t N, int64_t BT, int64_t D, int64_t S, int dtype, const DevInfo& di) {
   TilePlan p;
+  if (!SY_TUNE_BATCHED_REG) return p;
   const int es = esize_of(dtype);
   if (!es || N < 1 || N > kRegMaxN || S < 2 || S > kBatchedMaxS || D < 1 || D > kMaxD ||
       BT < 1 || BT > INT_MAX)
@@ -358,7 +363,7 @@ TilePlan plan_batched(int64_t N, int64_t BT, int64_t D, int64_t S, int dtype, co
     if (N * cand * vec > kBatchedTileFloats) continue;
     if (cand > 1 && rc < 32 * cand) continue;  // lanes would be idle
     const int64_t t = round32((rc + cand - 1) / cand);
-    if (t <= 256 && (rc + t - 1) / t <= cand) cpt = cand, tg = (int)t;
+    if (t <= kBatchedThreads && (rc + t - 1) / t <= cand) cpt = cand, tg = (int)t;
   }
   if (!cpt) return p;
   TileCfg c{};
@@ -374,12 +379,66 @@ TilePlan plan_batched(int64_t N, int64_t BT, int64_t D, int64_t S, int dtype, co
   DevInfo room = di;  // the queries take S rows of shared memory
   room.max_smem = di.max_smem - (int)(S * c.row_bytes) - 128;
   int64_t smem = 0;
-  if (room.max_smem <= 0 || !size_ring(c, kOpFwd, 256 / tg, room, &smem, true)) return p;
+  if (room.max_smem <= 0 || !size_ring(c, kOpFwd, kBatchedThreads / tg, room, &smem, true)) return p;
   p.kind = kPlanRegTile;
   p.c = c;
   p.cpt = cpt;
   p.grid = (int)(BT < di.sms ? BT : di.sms);
   p.smem = (int64_t)(batched_q_off(c) + (size_t)S * c.row_bytes);
+  return p;
+}
+
+struct StreamBatchedPlan {
+  bool ok = false;
+  StreamBatchedCfg c{};
+  int grid = 0;
+  int64_t smem = 0;
+};
+
+// Row-stream batched forward (the shapes the register tile cannot hold): rows
+// of exactly 32 * K chunks, K = 2 .. 16 warps per token (1 to 8 KiB rows at
+// two bytes per element), N <= 32, 2 <= S <= 16. Whole tokens per token
+// stream, as evenly as possible.
+StreamBatchedPlan plan_stream_batched(int64_t N, int64_t BT, int64_t D, int64_t S, int dtype,
+                                      const DevInfo& di) {
+  StreamBatchedPlan p;
+  const int es = esize_of(dtype);
+  if (!es || N < 1 || N > kStreamBatchedMaxN || S < 2 || S > kStreamBatchedMaxS || D < 1 ||
+      D > kMaxD || BT < 1 || BT > INT_MAX)
+    return p;
+  if ((D * es) % 16) return p;
+  const int64_t rc = D * es / 16;
+  if (rc % 32) return p;
+  const int64_t kw = rc / 32;
+  if (kw < 2 || kw > 16) return p;
+  const int64_t max_streams = kStreamBatchedThreads / 32 / kw;
+  const int64_t g0 = BT < di.sms ? BT : di.sms;
+  const int64_t t = (BT + g0 - 1) / g0;
+  const int64_t k = (t + max_streams - 1) / max_streams;
+  const int64_t streams = (t + k - 1) / k;
+  const int64_t ngrp = (S + kStreamBatchedQG - 1) / kStreamBatchedQG;
+  if (k * N * (1 + ngrp) >= (int64_t)INT_MAX) return p;  // stream rows are counted in 32 bits
+  StreamBatchedCfg c{};
+  c.BT = BT;
+  c.N = (int)N;
+  c.D = (int)D;
+  c.S = (int)S;
+  c.row_chunks = (int)rc;
+  c.row_bytes = (int)(D * es);
+  c.kw = (int)kw;
+  c.warps = (int)(streams * kw);
+  c.ring = 0;
+  const int64_t fixed = (int64_t)stream_batched_smem_layout(c).total;
+  const int64_t per_row = streams * ((int64_t)c.row_bytes + 8 + 4);
+  int64_t ring = (di.max_smem - fixed - 16) / per_row;
+  if (ring > 16) ring = 16;
+  if (ring < 2) return p;
+  c.ring = (int)ring;
+  p.smem = (int64_t)stream_batched_smem_layout(c).total;
+  if (p.smem > di.max_smem) return p;
+  p.c = c;
+  p.grid = (int)g0;
+  p.ok = true;
   return p;
 }
 
@@ -617,6 +676,13 @@ int sy_fwd_batched(const void* v, const void* queries, void* out, int64_t N, int
     e = launch_plan_batched(bp, (int)S, dtype, v, queries, out, static_cast<cudaStream_t>(stream));
     return cuda_status(e, "sy_fwd_batched: register-tile kernel launch");
   }
+  StreamBatchedPlan sb = plan_stream_batched(N, BT, D, S, dtype, di);
+  sb.c.eps = eps;
+  if (sb.ok && al16(v) && al16(queries) && al16(out)) {
+    e = launch_stream_batched(sb.c, sb.grid, dtype, v, queries, out,
+                              static_cast<cudaStream_t>(stream));
+    return cuda_status(e, "sy_fwd_batched: stream kernel launch");
+  }
   if (!generic_batched_fits(N, S, di)) return SY_ERR_UNSUPPORTED;
   e = launch_generic_batched(BT, (int)N, (int)D, (int)S, dtype, v, queries, out, eps,
                              generic_grid(BT, di), static_cast<cudaStream_t>(stream));
@@ -700,6 +766,20 @@ int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype,
     p = plan_tile(top, N, bt, D, dtype, di);
   else
     p = plan_batched(N, bt, D, S, dtype, di);
+  if (op == 2 && S > 1 && p.kind != kPlanRegTile) {
+    const StreamBatchedPlan sb = plan_stream_batched(N, bt, D, S, dtype, di);
+    if (sb.ok) {
+      out[0] = kPlanStream;
+      out[1] = sb.grid;
+      out[2] = sb.c.ring;
+      out[3] = sb.c.warps / sb.c.kw;  // token streams per CTA
+      out[4] = 32 * sb.c.kw;          // threads per token stream
+      out[5] = 1;                     // one chunk per lane
+      out[6] = sb.c.row_bytes;
+      out[7] = sb.smem;
+      return SY_OK;
+    }
+  }
   out[0] = p.kind;
   out[1] = p.grid;
   out[2] = p.c.stages;

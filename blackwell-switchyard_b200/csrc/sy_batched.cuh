@@ -26,7 +26,14 @@
 namespace sy {
 
 constexpr int kBatchedMaxS = 16;
-constexpr int kBatchedTileFloats = 144;  // fp32 tile per thread (N * CPT * VEC)
+#ifndef SY_TUNE_BATCHED_TILE
+#define SY_TUNE_BATCHED_TILE 144
+#endif
+#ifndef SY_TUNE_BATCHED_THREADS
+#define SY_TUNE_BATCHED_THREADS 256
+#endif
+constexpr int kBatchedTileFloats = SY_TUNE_BATCHED_TILE;  // fp32 tile per thread (N * CPT * VEC)
+constexpr int kBatchedThreads = SY_TUNE_BATCHED_THREADS;   // per CTA
 
 // Shared memory beyond the tile layout: the S query rows.
 __host__ __device__ inline size_t batched_q_off(const TileCfg& c) {
@@ -34,7 +41,7 @@ __host__ __device__ inline size_t batched_q_off(const TileCfg& c) {
 }
 
 template <typename T, int N, int CPT>
-__global__ void __launch_bounds__(256, 1)
+__global__ void __launch_bounds__(kBatchedThreads, 1)
     reg_batched_kernel(const T* __restrict__ v, const T* __restrict__ q, T* __restrict__ out,
                        const TileCfg c, int S) {
   constexpr int VEC = Dt<T>::kVec;
@@ -268,7 +275,7 @@ cudaError_t launch_batched_n(const TileCfg& c, int grid, int cpt, int S, const v
                              const void* q, void* out, cudaStream_t st) {
   const size_t smem = batched_q_off(c) + (size_t)S * c.row_bytes;
   const dim3 block(c.groups * c.tg);
-  if ((int)block.x > 256) return cudaErrorInvalidConfiguration;
+  if ((int)block.x > kBatchedThreads) return cudaErrorInvalidConfiguration;
   const T* vp = static_cast<const T*>(v);
   const T* qp = static_cast<const T*>(q);
   T* op = static_cast<T*>(out);

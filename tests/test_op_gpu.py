@@ -170,10 +170,11 @@ def test_dispatch_sends_the_representative_shape_to_the_tile_kernels():
     for n, d in ((9, 8192), (17, 4096), (17, 2048), (32, 4096)):
         assert _plan("bwd", n, 4096, d, torch.bfloat16) == PLAN_STREAM
     # batched queries: the register tile reused across queries; tiles that do
-    # not fit registers (N=17, D=4096) take the generic kernel
+    # not fit registers (N=17, D=4096) take the row-stream batched kernel
     for s in (2, 4, 8, 16):
         assert _plan("batched", 9, 4096, 2048, torch.bfloat16, s) == PLAN_TILE
-    assert _plan("batched", 17, 4096, 4096, torch.bfloat16, 8) == PLAN_GENERIC
+    assert _plan("batched", 17, 4096, 4096, torch.bfloat16, 8) == PLAN_STREAM
+    assert _plan("batched", 33, 4096, 4096, torch.bfloat16, 8) == PLAN_GENERIC  # N > 32
     # rows that are not a multiple of 16 bytes take the generic kernels
     assert _plan("fwd", 3, 64, 777, torch.bfloat16) == PLAN_GENERIC
     assert _plan("bwd", 5, 17, 63, torch.float32) == PLAN_GENERIC
@@ -276,6 +277,19 @@ def test_arena_alias_pattern():
 
 
 # ---------------------------------------------------------------- determinism
+
+
+def test_row_stream_batched_is_bit_stable():
+    v = randn(17, 1, 700, 4096, dtype=torch.bfloat16, seed=3)
+    q = randn(8, 4096, dtype=torch.bfloat16, seed=4, scale=4096 ** -0.5)
+    assert _plan("batched", 17, 700, 4096, torch.bfloat16, 8) == PLAN_STREAM
+    with torch.no_grad():
+        a = block_attn_res_batched(v, q)
+        b = block_attn_res_batched(v, q)
+    assert torch.equal(a, b)
+    toks = torch.arange(0, 700, 37)
+    want = O.batched(np64(v[:, :, toks]), np64(q))
+    assert O.rel_l2(np64(a[:, :, toks]), want) <= 1.005 * O.dtype_floor(want, "bfloat16")
 
 
 @pytest.mark.parametrize("shape", [(9, 1, 4096, 2048), (4, 2, 128, 512), (17, 1, 64, 2048), (3, 1, 64, 777)])

@@ -132,7 +132,11 @@ def test_backward_other_dtypes(shape, dtype):
 @pytest.mark.parametrize(
     ("shape", "n_queries"),
     [((2, 1, 7, 32), 2), ((5, 1, 17, 777), 3), ((9, 1, 16, 2048), 8), ((9, 1, 4, 4096), 4),
-     ((9, 1, 32, 2048), 16), ((17, 1, 8, 4096), 8), ((9, 1, 8, 2048), 1), ((3, 2, 5, 64), 5)],
+     ((9, 1, 32, 2048), 16), ((17, 1, 8, 4096), 8), ((9, 1, 8, 2048), 1), ((3, 2, 5, 64), 5),
+     # the row-stream batched kernel: several tokens per stream, S = 16 (32-wide
+     # reduce-scatter), S = 9 (two sweeps of pass B), N up to 32
+     ((20, 1, 300, 2048), 16), ((17, 1, 200, 4096), 3), ((24, 1, 160, 1024), 9),
+     ((32, 2, 80, 1024), 2)],
 )
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_batched_forward_is_at_the_dtype_floor(shape, n_queries, dtype):
