@@ -395,10 +395,11 @@ struct StreamBatchedPlan {
   int64_t smem = 0;
 };
 
-// Row-stream batched forward (the shapes the register tile cannot hold): rows
-// of exactly 32 * K chunks, K = 2 .. 16 warps per token (1 to 8 KiB rows at
-// two bytes per element), N <= 32, 2 <= S <= 16. Whole tokens per token
-// stream, as evenly as possible.
+// Row-stream batched forward (the shapes the register tile cannot hold): S
+// queries in SB = 4, 8 or 16 slots, CPL = 1 or 2 chunks per lane (2 when the
+// queries' registers, SB * CPL 16-byte chunks, stay within 16), rows of exactly
+// 32 * CPL * K chunks with K = 2 .. 16 warps per token, N <= 32. Whole tokens
+// per token stream, as evenly as possible.
 StreamBatchedPlan plan_stream_batched(int64_t N, int64_t BT, int64_t D, int64_t S, int dtype,
                                       const DevInfo& di) {
   StreamBatchedPlan p;
@@ -408,16 +409,24 @@ StreamBatchedPlan plan_stream_batched(int64_t N, int64_t BT, int64_t D, int64_t 
     return p;
   if ((D * es) % 16) return p;
   const int64_t rc = D * es / 16;
-  if (rc % 32) return p;
-  const int64_t kw = rc / 32;
-  if (kw < 2 || kw > 16) return p;
+  const int sb = S <= 4 ? 4 : (S <= 8 ? 8 : 16);
+  int cpl = 0;
+  for (int cand = 2; cand >= 1 && !cpl; cand /= 2) {  // (4 chunks per lane spill)
+    if (sb * cand > 16 || rc % (32 * cand)) continue;
+    const int64_t k = rc / (32 * cand);
+    if (k >= 2 && k <= 16) cpl = cand;
+  }
+  if (!cpl) return p;
+  const int64_t kw = rc / (32 * cpl);
   const int64_t max_streams = kStreamBatchedThreads / 32 / kw;
   const int64_t g0 = BT < di.sms ? BT : di.sms;
   const int64_t t = (BT + g0 - 1) / g0;
   const int64_t k = (t + max_streams - 1) / max_streams;
-  const int64_t streams = (t + k - 1) / k;
-  const int64_t ngrp = (S + kStreamBatchedQG - 1) / kStreamBatchedQG;
-  if (k * N * (1 + ngrp) >= (int64_t)INT_MAX) return p;  // stream rows are counted in 32 bits
+  int64_t streams = (t + k - 1) / k;
+  if (streams > 8) streams = 8;  // named barrier ids 1..8
+  const int64_t qg = stream_batched_qg(cpl);
+  const int64_t ngrp = (S + qg - 1) / qg;
+  if (((t + streams - 1) / streams) * N * (1 + ngrp) >= (int64_t)INT_MAX) return p;
   StreamBatchedCfg c{};
   c.BT = BT;
   c.N = (int)N;
@@ -426,6 +435,8 @@ StreamBatchedPlan plan_stream_batched(int64_t N, int64_t BT, int64_t D, int64_t 
   c.row_chunks = (int)rc;
   c.row_bytes = (int)(D * es);
   c.kw = (int)kw;
+  c.cpl = cpl;
+  c.sb = sb;
   c.warps = (int)(streams * kw);
   c.ring = 0;
   const int64_t fixed = (int64_t)stream_batched_smem_layout(c).total;
@@ -774,7 +785,7 @@ int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype,
       out[2] = sb.c.ring;
       out[3] = sb.c.warps / sb.c.kw;  // token streams per CTA
       out[4] = 32 * sb.c.kw;          // threads per token stream
-      out[5] = 1;                     // one chunk per lane
+      out[5] = sb.c.cpl;              // chunks per lane
       out[6] = sb.c.row_bytes;
       out[7] = sb.smem;
       return SY_OK;

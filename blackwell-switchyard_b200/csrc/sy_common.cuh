@@ -180,8 +180,24 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
                : "memory");
 }
 
+// Suspend-time hint of the waits, in ns (0: none). With a hint a waiting
+// thread sleeps until the phase completes or the hint elapses, instead of
+// returning at once and spinning (issue slots the working warps need).
+#ifndef SY_TUNE_WAIT_HINT_NS
+#define SY_TUNE_WAIT_HINT_NS 0
+#endif
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
+#if SY_TUNE_WAIT_HINT_NS > 0
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "n"(SY_TUNE_WAIT_HINT_NS)
+      : "memory");
+#else
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
@@ -189,19 +205,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "=r"(ok)
       : "r"(bar), "r"(parity)
       : "memory");
+#endif
   return ok != 0;
 }
 
 // Wait for the phase with the given parity to complete. Bounded: after
 // kWaitLimitNs it records kDevErrWaitTimeout and returns false; the caller
-// then stops issuing work and returns.
+// then stops issuing work and returns. (With a suspend hint every attempt can
+// sleep, so the clock is read after every failed attempt.)
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(a, parity)) return true;
-    if ((it & 255u) == 0 && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((SY_TUNE_WAIT_HINT_NS > 0 || (it & 255u) == 0) && globaltimer_ns() - t0 > kWaitLimitNs) {
       record_device_error(kDevErrWaitTimeout);
       return false;
     }

@@ -557,6 +557,8 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
   const int cb = wk * 256 + lane;  // this lane's chunks: cb + 32k
   const float inv_d = 1.f / (float)c.D;
   int q = 0;
+  int ring_slot = 0;  // slot and phase of stream row q (q mod R, (q / R) & 1)
+  uint32_t ring_ph = 0;
   for (int j = 0; j < ntok; ++j) {
     float2 o[CPL][P];
 #pragma unroll
@@ -567,8 +569,13 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
     float lane_logit = 0.f, lane_r = 0.f;  // row `lane`'s statistics (warp 0 of the stream)
     float* st = stats != nullptr ? stats + (tok0 + tstride * j) * c.stats_stride : nullptr;
     for (int n = 0; n < c.N; ++n, ++q) {
-      const int slot = q % c.ring;
-      if (!mbar_wait(&bar[slot], (uint32_t)((q / c.ring) & 1))) return;
+      const int slot = ring_slot;
+      const uint32_t ph = ring_ph;
+      if (++ring_slot == c.ring) {
+        ring_slot = 0;
+        ring_ph ^= 1u;
+      }
+      if (!mbar_wait(&bar[slot], ph)) return;
       const unsigned char* row = ring + (size_t)slot * RB;
       // pass 1: this warp's part of dot and sum of squares
       float2 dacc[2], sacc[2];

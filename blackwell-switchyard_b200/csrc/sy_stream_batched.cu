@@ -3,19 +3,34 @@
 
 namespace sy {
 
+template <typename T, int SB, int CPL>
+static cudaError_t launch_sb(const StreamBatchedCfg& c, int grid, const void* v, const void* q,
+                             void* out, cudaStream_t st) {
+  return launch_smem(stream_batched_kernel<T, SB, CPL>, grid, dim3(c.warps * 32),
+                     stream_batched_smem_layout(c).total, st, static_cast<const T*>(v),
+                     static_cast<const T*>(q), static_cast<T*>(out), c);
+}
+
+// (query slots, chunks per lane): the planner keeps SB * CPL <= 16 (the queries'
+// registers in pass A).
 template <typename T>
 static cudaError_t launch_stream_batched_t(const StreamBatchedCfg& c, int grid, const void* v,
                                            const void* q, void* out, cudaStream_t st) {
   if (c.warps * 32 > kStreamBatchedThreads) return cudaErrorInvalidConfiguration;
-  const size_t smem = stream_batched_smem_layout(c).total;
-  const T* vp = static_cast<const T*>(v);
-  const T* qp = static_cast<const T*>(q);
-  T* op = static_cast<T*>(out);
-  if (c.S + 1 <= 16)
-    return launch_smem(stream_batched_kernel<T, 16>, grid, dim3(c.warps * 32), smem, st, vp, qp,
-                       op, c);
-  return launch_smem(stream_batched_kernel<T, 32>, grid, dim3(c.warps * 32), smem, st, vp, qp, op,
-                     c);
+  switch (c.sb * 8 + c.cpl) {
+    case 4 * 8 + 2:
+      return launch_sb<T, 4, 2>(c, grid, v, q, out, st);
+    case 4 * 8 + 1:
+      return launch_sb<T, 4, 1>(c, grid, v, q, out, st);
+    case 8 * 8 + 2:
+      return launch_sb<T, 8, 2>(c, grid, v, q, out, st);
+    case 8 * 8 + 1:
+      return launch_sb<T, 8, 1>(c, grid, v, q, out, st);
+    case 16 * 8 + 1:
+      return launch_sb<T, 16, 1>(c, grid, v, q, out, st);
+    default:
+      return cudaErrorInvalidValue;
+  }
 }
 
 cudaError_t launch_stream_batched(const StreamBatchedCfg& c, int grid, int dtype, const void* v,

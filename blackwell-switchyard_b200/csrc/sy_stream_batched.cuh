@@ -2,21 +2,21 @@
 // cannot hold (more than 16 sources, or rows too long for the tile at N > 9).
 //
 // out[s] = sum_n softmax_n(q_s . k_n) v_n for S <= 16 queries, k_n = v_n r_n,
-// r_n = rsqrt(mean(v_n^2) + eps). K = D * itemsize / 512 warps share a token,
-// one 16-byte chunk per lane, and the token's rows stream through the K warps'
+// r_n = rsqrt(mean(v_n^2) + eps). K warps share a token, CPL 16-byte chunks
+// per lane (K = D * itemsize / (512 CPL)), and the token's rows stream through the K warps'
 // shared ring of row buffers (cp.async.bulk, one mbarrier each) twice:
 //
 //   pass A   v_0 .. v_{N-1} from HBM (evict-last hint): per row, the lane's
 //            part of v_n . v_n and of q_s . v_n for every query (queries in
 //            registers, loaded once per token from shared memory), one
-//            reduce-scatter over the warp, the warp's S + 1 sums to shared
-//            memory;
+//            reduce-scatter over the warp for every 32 / (S + 1) rows, the
+//            warp's S + 1 sums per row to shared memory;
 //   reduce   the K warps' sums added in warp order (named barrier), then one
 //            warp per query: logits in lanes n < N, softmax, alpha_{s,n} to
 //            shared memory;
-//   pass B   v_0 .. v_{N-1} again (normally from L2, evict-first), per 8
+//   pass B   v_0 .. v_{N-1} again (normally from L2, evict-first), per 8 / CPL
 //            queries: out[s] += alpha_{s,n} v_n in fp32 registers, one 16-byte
-//            store per query and lane at the end (S > 8: a second sweep).
+//            store per query and chunk at the end (more queries: more sweeps).
 //
 // HBM traffic is the minimum, (N + S) rows per token; pass B's re-read stays
 // on chip. Reference: the batched forward of src/switchyard/triton_op.py:
@@ -31,9 +31,11 @@ namespace sy {
 struct StreamBatchedCfg {
   long long BT;
   int N, D, S;
-  int row_chunks;  // 16-byte chunks per row: exactly 32 * kw
+  int row_chunks;  // 16-byte chunks per row: exactly 32 * cpl * kw
   int row_bytes;
   int kw;          // warps per token
+  int cpl;         // chunks per lane (1, 2 or 4)
+  int sb;          // query slots (4, 8 or 16; S <= sb, the rest are zero queries)
   int warps;       // per CTA, a multiple of kw
   int ring;        // row buffers per token stream
   float eps;
@@ -42,7 +44,8 @@ struct StreamBatchedCfg {
 constexpr int kStreamBatchedThreads = 512;
 constexpr int kStreamBatchedMaxN = 32;  // lane n holds source n in the softmax
 constexpr int kStreamBatchedMaxS = 16;
-constexpr int kStreamBatchedQG = 8;     // queries per pass-B sweep (8 x 8 fp32 accumulators)
+// pass B keeps 8 fp32 values per query and chunk: 8 / cpl queries per sweep
+__host__ __device__ constexpr int stream_batched_qg(int cpl) { return 8 / cpl; }
 
 struct StreamBatchedSmem {
   size_t q_off, ring_off, bar_off, red_off, tot_off, alpha_off, cnt_off, total;
@@ -67,15 +70,18 @@ __host__ __device__ inline StreamBatchedSmem stream_batched_smem_layout(const St
   return s;
 }
 
-// M: the reduce-scatter width, 16 (S <= 15) or 32 (S = 16).
-template <typename T, int M>
+// SB query slots, CPL chunks per lane. Pass A reduces RR = 32 / (SB + 1) rows
+// per 32-wide reduce-scatter (3 at SB = 8).
+template <typename T, int SB, int CPL>
 __global__ void __launch_bounds__(kStreamBatchedThreads, 1)
     stream_batched_kernel(const T* __restrict__ v, const T* __restrict__ q, T* __restrict__ out,
                           const StreamBatchedCfg c) {
   constexpr int VEC = Dt<T>::kVec;
   constexpr int P = VEC / 2;
-  constexpr int QG = kStreamBatchedQG;
-  constexpr int SMAX = kStreamBatchedMaxS;
+  constexpr int QG = stream_batched_qg(CPL);
+  constexpr int W = SB + 1;   // values per row: v.v and SB dots
+  constexpr int RR = 32 / W;  // rows per reduce-scatter
+  static_assert(RR >= 1, "too many query slots");
   const StreamBatchedSmem L = stream_batched_smem_layout(c);
   unsigned char* qsm = sy_smem + L.q_off;
   unsigned char* ring0 = sy_smem + L.ring_off;
@@ -87,8 +93,9 @@ __global__ void __launch_bounds__(kStreamBatchedThreads, 1)
   const int K = c.kw, S = c.S, N = c.N, V = c.S + 1;
   const int RB = c.row_bytes;
   if (K < 2 || K > 16 || c.warps % K != 0 || c.warps != (int)(blockDim.x >> 5) ||
-      c.warps / K > 8 || c.ring < 2 || c.row_chunks != 32 * K || RB != 16 * c.row_chunks ||
-      N < 1 || N > kStreamBatchedMaxN || S < 2 || S > SMAX || V > M) {
+      c.warps / K > 8 || c.ring < 2 || c.cpl != CPL || c.sb != SB ||
+      c.row_chunks != 32 * CPL * K || RB != 16 * c.row_chunks || N < 1 ||
+      N > kStreamBatchedMaxN || S < 2 || S > SB) {
     if (tid == 0) record_device_error(kDevErrBadPlan);
     return;
   }
@@ -148,68 +155,96 @@ __global__ void __launch_bounds__(kStreamBatchedThreads, 1)
   if (wk == 0 && lane == 0)
     for (int s = 0; s < c.ring; ++s) issue_row(s, s);
 
-  const int ch = wk * 32 + lane;  // this lane's chunk of every row
+  const int cb = wk * 32 * CPL + lane;  // this lane's chunks: cb + 32k
   const float inv_d = 1.f / (float)c.D;
   bool ok = true;
   int r = 0;
+  int ring_slot = 0;        // slot and phase of stream row r (r mod R, (r / R) & 1)
+  uint32_t ring_ph = 0;
   for (int j = 0; j < ntok && ok; ++j) {
     const long long tok = tok0 + tstride * j;
     // ---- pass A: v_n . v_n and q_s . v_n, this warp's part ----
-    uint4 qr[SMAX];
+    uint4 qr[SB][CPL];  // zero beyond S
 #pragma unroll
-    for (int s = 0; s < SMAX; ++s)
-      qr[s] = s < S ? lds128(qsm + (size_t)s * RB + ch * 16) : make_uint4(0u, 0u, 0u, 0u);
-    for (int n = 0; n < N; ++n, ++r) {
-      const int slot = r % c.ring;
-      if (!mbar_wait(&bar[slot], (uint32_t)((r / c.ring) & 1))) {
-        ok = false;
-        break;
-      }
-      const uint4 xu = lds128(ring + (size_t)slot * RB + ch * 16);
-      release(slot, r);
-      float a[M];
+    for (int s = 0; s < SB; ++s)
 #pragma unroll
-      for (int i = 0; i < M; ++i) a[i] = 0.f;
-      if constexpr (sizeof(T) == 2) {
-        float2 acc = make_float2(0.f, 0.f);
-        mixfma2<T>(acc, xu.x, xu.x);
-        mixfma2<T>(acc, xu.y, xu.y);
-        mixfma2<T>(acc, xu.z, xu.z);
-        mixfma2<T>(acc, xu.w, xu.w);
-        a[0] = acc.x + acc.y;
+      for (int k = 0; k < CPL; ++k)
+        qr[s][k] = s < S ? lds128(qsm + (size_t)s * RB + (cb + 32 * k) * 16)
+                         : make_uint4(0u, 0u, 0u, 0u);
+    for (int n0 = 0; n0 < N && ok; n0 += RR) {
+      float a[32];
 #pragma unroll
-        for (int s = 0; s < SMAX && s + 1 < M; ++s) {
-          if (s < S) {
-            float2 d = make_float2(0.f, 0.f);
-            mixfma2<T>(d, qr[s].x, xu.x);
-            mixfma2<T>(d, qr[s].y, xu.y);
-            mixfma2<T>(d, qr[s].z, xu.z);
-            mixfma2<T>(d, qr[s].w, xu.w);
-            a[1 + s] = d.x + d.y;
+      for (int i = 0; i < 32; ++i) a[i] = 0.f;
+#pragma unroll
+      for (int rr = 0; rr < RR; ++rr) {
+        if (n0 + rr < N) {  // warp-uniform
+          const int slot = ring_slot;
+          const uint32_t ph = ring_ph;
+          if (++ring_slot == c.ring) {
+            ring_slot = 0;
+            ring_ph ^= 1u;
+          }
+          if (!mbar_wait(&bar[slot], ph)) {
+            ok = false;
+            break;
+          }
+          uint4 xu[CPL];
+#pragma unroll
+          for (int k = 0; k < CPL; ++k) xu[k] = lds128(ring + (size_t)slot * RB + (cb + 32 * k) * 16);
+          release(slot, r);
+          ++r;
+          if constexpr (sizeof(T) == 2) {
+            float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+            for (int k = 0; k < CPL; ++k) {
+              mixfma2<T>(acc, xu[k].x, xu[k].x);
+              mixfma2<T>(acc, xu[k].y, xu[k].y);
+              mixfma2<T>(acc, xu[k].z, xu[k].z);
+              mixfma2<T>(acc, xu[k].w, xu[k].w);
+            }
+            a[rr * W] = acc.x + acc.y;
+#pragma unroll
+            for (int s = 0; s < SB; ++s) {
+              float2 d = make_float2(0.f, 0.f);
+#pragma unroll
+              for (int k = 0; k < CPL; ++k) {
+                mixfma2<T>(d, qr[s][k].x, xu[k].x);
+                mixfma2<T>(d, qr[s][k].y, xu[k].y);
+                mixfma2<T>(d, qr[s][k].z, xu[k].z);
+                mixfma2<T>(d, qr[s][k].w, xu[k].w);
+              }
+              a[rr * W + 1 + s] = d.x + d.y;
+            }
+          } else {
+            float2 acc = make_float2(0.f, 0.f);
+            float2 x[CPL][P];
+#pragma unroll
+            for (int k = 0; k < CPL; ++k) {
+              unpack2<T>(xu[k], x[k]);
+#pragma unroll
+              for (int i = 0; i < P; ++i) acc = __ffma2_rn(x[k][i], x[k][i], acc);
+            }
+            a[rr * W] = acc.x + acc.y;
+#pragma unroll
+            for (int s = 0; s < SB; ++s) {
+              float2 d = make_float2(0.f, 0.f);
+#pragma unroll
+              for (int k = 0; k < CPL; ++k) {
+                float2 qf[P];
+                unpack2<T>(qr[s][k], qf);
+#pragma unroll
+                for (int i = 0; i < P; ++i) d = __ffma2_rn(qf[i], x[k][i], d);
+              }
+              a[rr * W + 1 + s] = d.x + d.y;
+            }
           }
         }
-      } else {
-        float2 x[P];
-        unpack2<T>(xu, x);
-        float2 acc = make_float2(0.f, 0.f);
-#pragma unroll
-        for (int i = 0; i < P; ++i) acc = __ffma2_rn(x[i], x[i], acc);
-        a[0] = acc.x + acc.y;
-#pragma unroll
-        for (int s = 0; s < SMAX && s + 1 < M; ++s) {
-          if (s < S) {
-            float2 qf[P];
-            unpack2<T>(qr[s], qf);
-            float2 d = make_float2(0.f, 0.f);
-#pragma unroll
-            for (int i = 0; i < P; ++i) d = __ffma2_rn(qf[i], x[i], d);
-            a[1 + s] = d.x + d.y;
-          }
-        }
       }
-      const float tl = warp_reduce_scatter<M>(a, lane);
-      const int vi = rs_index<M>(lane);
-      if (vi < V && (M == 32 || (lane & 1) == 0)) red[((size_t)n * K + wk) * V + vi] = tl;
+      if (!ok) break;
+      // lane L: the warp's sum of value L = (row n0 + L / W, value L mod W)
+      const float tl = warp_reduce_scatter<32>(a, lane);
+      const int rr = lane / W, i = lane - rr * W;
+      if (rr < RR && n0 + rr < N && i < V) red[((size_t)(n0 + rr) * K + wk) * V + i] = tl;
     }
     if (!ok) break;
     named_sync(1 + gi, 32 * K);
@@ -239,22 +274,31 @@ __global__ void __launch_bounds__(kStreamBatchedThreads, 1)
     }
     named_sync(1 + gi, 32 * K);
 
-    // ---- pass B: up to QG queries per sweep over the rows ----
+    // ---- pass B: QG queries per sweep over the rows ----
     for (int g0 = 0; g0 < S && ok; g0 += QG) {
       const int qn = S - g0 < QG ? S - g0 : QG;
-      float2 o[QG][P];
+      float2 o[QG][CPL][P];
 #pragma unroll
       for (int qq = 0; qq < QG; ++qq)
 #pragma unroll
-        for (int i = 0; i < P; ++i) o[qq][i] = make_float2(0.f, 0.f);
+        for (int k = 0; k < CPL; ++k)
+#pragma unroll
+          for (int i = 0; i < P; ++i) o[qq][k][i] = make_float2(0.f, 0.f);
       for (int n = 0; n < N; ++n, ++r) {
-        const int slot = r % c.ring;
-        if (!mbar_wait(&bar[slot], (uint32_t)((r / c.ring) & 1))) {
+        const int slot = ring_slot;
+        const uint32_t ph = ring_ph;
+        if (++ring_slot == c.ring) {
+          ring_slot = 0;
+          ring_ph ^= 1u;
+        }
+        if (!mbar_wait(&bar[slot], ph)) {
           ok = false;
           break;
         }
-        float2 x[P];
-        unpack2<T>(lds128(ring + (size_t)slot * RB + ch * 16), x);
+        float2 x[CPL][P];
+#pragma unroll
+        for (int k = 0; k < CPL; ++k)
+          unpack2<T>(lds128(ring + (size_t)slot * RB + (cb + 32 * k) * 16), x[k]);
         release(slot, r);
         const float* ap = alpha + (size_t)g0 * N + n;
 #pragma unroll
@@ -262,7 +306,9 @@ __global__ void __launch_bounds__(kStreamBatchedThreads, 1)
           if (qq < qn) {
             const float al = ap[(size_t)qq * N];
 #pragma unroll
-            for (int i = 0; i < P; ++i) o[qq][i] = __ffma2_rn(f2(al), x[i], o[qq][i]);
+            for (int k = 0; k < CPL; ++k)
+#pragma unroll
+              for (int i = 0; i < P; ++i) o[qq][k][i] = __ffma2_rn(f2(al), x[k][i], o[qq][k][i]);
           }
         }
       }
@@ -270,7 +316,10 @@ __global__ void __launch_bounds__(kStreamBatchedThreads, 1)
 #pragma unroll
       for (int qq = 0; qq < QG; ++qq)
         if (qq < qn)
-          stg128(out + ((size_t)(g0 + qq) * c.BT + tok) * c.D + (size_t)ch * VEC, pack2<T>(o[qq]));
+#pragma unroll
+          for (int k = 0; k < CPL; ++k)
+            stg128(out + ((size_t)(g0 + qq) * c.BT + tok) * c.D + (size_t)(cb + 32 * k) * VEC,
+                   pack2<T>(o[qq][k]));
     }
   }
 }

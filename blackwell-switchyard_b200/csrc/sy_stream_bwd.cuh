@@ -182,6 +182,8 @@ __global__ void __launch_bounds__(kStreamBwdThreads, 1)
 
   bool ok = true;
   int q = 0;
+  int ring_slot = 0;        // slot and phase of stream row q (q mod R, (q / R) & 1)
+  uint32_t ring_ph = 0;
   for (int j = 0; j < ntok && ok; ++j) {
     const long long tok = tok0 + tstride * j;
     // lane n < N: source n's saved logit and inverse RMS (used after pass A)
@@ -193,8 +195,13 @@ __global__ void __launch_bounds__(kStreamBwdThreads, 1)
     // ---- g: to registers as fp32 ----
     float2 gf[CPL][P];
     {
-      const int slot = q % c.ring;
-      if (!mbar_wait(&bar[slot], (uint32_t)((q / c.ring) & 1))) {
+      const int slot = ring_slot;
+      const uint32_t ph = ring_ph;
+      if (++ring_slot == c.ring) {
+        ring_slot = 0;
+        ring_ph ^= 1u;
+      }
+      if (!mbar_wait(&bar[slot], ph)) {
         ok = false;
         break;
       }
@@ -208,8 +215,13 @@ __global__ void __launch_bounds__(kStreamBwdThreads, 1)
     // ---- pass A: this warp's part of G_n = g . v_n, lane n keeps it ----
     float myg = 0.f;
     for (int n = 0; n < N; ++n, ++q) {
-      const int slot = q % c.ring;
-      if (!mbar_wait(&bar[slot], (uint32_t)((q / c.ring) & 1))) {
+      const int slot = ring_slot;
+      const uint32_t ph = ring_ph;
+      if (++ring_slot == c.ring) {
+        ring_slot = 0;
+        ring_ph ^= 1u;
+      }
+      if (!mbar_wait(&bar[slot], ph)) {
         ok = false;
         break;
       }
@@ -251,8 +263,13 @@ __global__ void __launch_bounds__(kStreamBwdThreads, 1)
       const float ka = __shfl_sync(kFull, alpha, n);
       const float kd = __shfl_sync(kFull, da_l, n);
       const float kc = __shfl_sync(kFull, cv_l, n);
-      const int slot = q % c.ring;
-      if (!mbar_wait(&bar[slot], (uint32_t)((q / c.ring) & 1))) {
+      const int slot = ring_slot;
+      const uint32_t ph = ring_ph;
+      if (++ring_slot == c.ring) {
+        ring_slot = 0;
+        ring_ph ^= 1u;
+      }
+      if (!mbar_wait(&bar[slot], ph)) {
         ok = false;
         break;
       }

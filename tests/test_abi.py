@@ -152,10 +152,12 @@ def test_planner_invariants_for_b200(native, dtype_name):
         p = native.plan_info(1, n, 4096, d, 1, torch.bfloat16, **B200)
         assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw and p["stages"] >= 3
     # batched queries beyond the register tile: the row-stream batched kernel,
-    # K = rows / 512 B warps per token, one chunk per lane
-    for n, d, s, kw in ((17, 4096, 8, 16), (20, 2048, 16, 8), (32, 1024, 2, 4)):
+    # K warps per token, as many chunks per lane as the queries' registers allow
+    for n, d, s, kw, cpl in ((17, 4096, 8, 8, 2), (20, 2048, 16, 8, 1), (32, 1024, 2, 2, 2),
+                             (17, 4096, 3, 8, 2)):
         p = native.plan_info(2, n, 4096, d, s, torch.bfloat16, **B200)
-        assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw and p["chunks_per_thread"] == 1
+        assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw
+        assert p["chunks_per_thread"] == cpl
         assert p["groups"] * p["threads_per_group"] <= 512 and p["stages"] >= 2
         assert p["smem_bytes"] <= B200["max_smem"]
     # rows that are not a multiple of 16 bytes go to the generic kernels
