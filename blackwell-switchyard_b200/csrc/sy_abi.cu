@@ -281,8 +281,11 @@ StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInf
   if (ring > 8) ring = 8;
   if (ring < 2) return p;
   c.ring = (int)ring;
-  p.smem = (int64_t)stream_smem_layout(c).total;
+  const StreamSmem lay = stream_smem_layout(c);
+  p.smem = (int64_t)lay.total;
   if (p.smem > di.max_smem) return p;
+  // 16-byte vector accesses and bulk copies: every region on a 16-byte boundary
+  if (lay.ring_off % 16 || lay.bar_off % 16 || lay.xch_off % 16 || lay.zero_off % 16) return p;
   const int64_t need = (BT + c.warps - 1) / c.warps;  // CTAs with work for every warp
   p.grid = (int)(need < di.sms ? need : di.sms);
   if (c.reread) p.grid = (int)(BT < di.sms ? BT : di.sms);

@@ -57,7 +57,9 @@ __host__ __device__ inline StreamSmem stream_smem_layout(const StreamCfg& c) {
   s.w_off = 0;                                                   // fp32 w[D]
   s.ring_off = ((size_t)c.D * 4 + 127) / 128 * 128;              // streams * R rows
   s.bar_off = s.ring_off + streams * c.ring * c.row_bytes;
-  s.xch_off = s.bar_off + streams * c.ring * 8;                  // float2 [streams][2][kw]
+  // the full barriers plus w's, rounded up to 16 bytes (the zero pad below is
+  // read and written as one 16-byte vector)
+  s.xch_off = s.bar_off + ((streams * c.ring + 1) * 8 + 15) / 16 * 16;  // float2 [streams][2][kw]
   s.cnt_off = s.xch_off + (kw > 1 ? streams * 2 * kw * 8 : 0);   // int [streams][R]
   s.zero_off = s.cnt_off + (kw > 1 ? (streams * c.ring * 4 + 15) / 16 * 16 : 0);
   s.total = s.zero_off + 16;
@@ -315,14 +317,22 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
     if (tid == 0) record_device_error(kDevErrBadPlan);
     return;
   }
+  // A 16-bit w in the sources' type (MIX) is already in the row layout: one
+  // bulk copy, the first in the queue, so the rings start filling at once.
+  // Otherwise w is staged by the threads before the rings start filling
+  // (issued after the bulk copies, its loads would wait behind them).
+  uint64_t* wbar = bars + c.warps * c.ring;
+  const bool wtma = MIX && (reinterpret_cast<uintptr_t>(w) & 15u) == 0;
   if (tid == 0) {
-    for (int i = 0; i < c.warps * c.ring; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < c.warps * c.ring + 1; ++i) mbar_init(&bars[i], 1);
     *reinterpret_cast<uint4*>(sy_smem + L.zero_off) = make_uint4(0u, 0u, 0u, 0u);
     mbar_fence_init();
+    if (wtma) {
+      mbar_arrive_expect_tx(wbar, (uint32_t)c.row_bytes);
+      bulk_g2s(wsm, w, (uint32_t)c.row_bytes, wbar, policy_evict_last());
+    }
   }
-  // w is staged before the rings start filling: issued after the bulk copies,
-  // its loads would wait behind them.
-  stage_w<T, MIX>(wsm, w, w_dtype, c.D, c.row_chunks);
+  if (!wtma) stage_w<T, MIX>(wsm, w, w_dtype, c.D, c.row_chunks);
   __syncthreads();
 
   // This warp's tokens: tok0 + tstride * j, j < ntok (fewer than 2^31 rows
@@ -351,6 +361,7 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
     }
   };
   for (int s = 0; s < c.ring; ++s) issue_next(s);
+  if (wtma && !mbar_wait(wbar, 0u)) return;
 
   auto cval = [&](int k) { return FULL || lane + 32 * k < RC; };
   const float inv_d = 1.f / (float)c.D;
@@ -524,12 +535,18 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
     if (tid == 0) record_device_error(kDevErrBadPlan);
     return;
   }
+  uint64_t* wbar = bars + streams * c.ring;  // w as one bulk copy (see the re-read kernel)
+  const bool wtma = MIX && (reinterpret_cast<uintptr_t>(w) & 15u) == 0;
   if (tid == 0) {
-    for (int i = 0; i < streams * c.ring; ++i) mbar_init(&bars[i], 1);
+    for (int i = 0; i < streams * c.ring + 1; ++i) mbar_init(&bars[i], 1);
     mbar_fence_init();
+    if (wtma) {
+      mbar_arrive_expect_tx(wbar, (uint32_t)RB);
+      bulk_g2s(wsm, w, (uint32_t)RB, wbar, policy_evict_last());
+    }
   }
   for (int i = tid; i < streams * c.ring; i += blockDim.x) cnt0[i] = 0;
-  stage_w<T, MIX>(wsm, w, w_dtype, c.D, RC);
+  if (!wtma) stage_w<T, MIX>(wsm, w, w_dtype, c.D, RC);
   __syncthreads();
 
   const int gi = wi / K, wk = wi - gi * K;
@@ -553,6 +570,7 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
   };
   if (wk == 0 && lane == 0)
     for (int s = 0; s < c.ring; ++s) issue_row(s, s);
+  if (wtma && !mbar_wait(wbar, 0u)) return;
 
   const int cb = wk * 256 + lane;  // this lane's chunks: cb + 32k
   const float inv_d = 1.f / (float)c.D;
