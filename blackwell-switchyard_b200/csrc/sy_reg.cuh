@@ -473,12 +473,8 @@ __global__ void __launch_bounds__(reg_threads(N, CPT, Dt<T>::kVec, true), 1)
   const unsigned char* gb = reinterpret_cast<const unsigned char*>(gin);
   const int st_bytes = c.stats_stride * 4;
 
-  if (tig == 0)
-    for (int j = 0; j < ring.cnt && j < ntok_g; ++j)
-      issue_token(stage0 + (size_t)(ring.base + j) * c.stage_bytes, &full[ring.base + j], vb,
-                  cta + (long long)(g + j * c.groups) * grid, N, c.row_bytes, nstride, gb, stats,
-                  st_bytes, pol);
-
+  // w's loads go out before the ring fill (issued after it, they would wait
+  // behind the bulk copies); they are first needed in phase B.
   bool cv[CPT];
   float2 w2[CPT][P], dw2[CPT][P];
 #pragma unroll
@@ -494,6 +490,12 @@ __global__ void __launch_bounds__(reg_threads(N, CPT, Dt<T>::kVec, true), 1)
     }
   }
   const float inv_d = 1.f / (float)c.D;
+
+  if (tig == 0)
+    for (int j = 0; j < ring.cnt && j < ntok_g; ++j)
+      issue_token(stage0 + (size_t)(ring.base + j) * c.stage_bytes, &full[ring.base + j], vb,
+                  cta + (long long)(g + j * c.groups) * grid, N, c.row_bytes, nstride, gb, stats,
+                  st_bytes, pol);
 
   int slot = 0;
   uint32_t ph = 0;
