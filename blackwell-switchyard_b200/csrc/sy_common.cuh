@@ -264,6 +264,16 @@ __device__ __forceinline__ uint64_t policy_evict_last() {
   return p;
 }
 
+// Programmatic dependent launch. pdl_trigger: the next kernel on the stream
+// (if launched as a programmatic dependent) may launch once every CTA of this
+// one has triggered or exited. pdl_wait: block until the previous kernel on
+// the stream has completed and its writes are visible (a no-op when this
+// kernel was launched normally); called before a kernel's first global read.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Order this thread's (and, through a preceding barrier, its group's)
 // generic-proxy reads of shared memory before async-proxy (bulk copy) writes
 // to the same bytes.

@@ -245,6 +245,7 @@ __global__ void __launch_bounds__(HOLD ? kHoldThreads : reg_threads(N, CPT, Dt<T
       issue_token(stage0 + (size_t)(ring.base + j) * c.stage_bytes, &full[ring.base + j], vb,
                   cta + (long long)(g + j * c.groups) * grid, N, c.row_bytes, nstride, nullptr,
                   nullptr, 0, pol);
+  pdl_trigger();  // every CTA is resident: the next kernel may queue for the SMs
 
   bool cv[CPT];
 #pragma unroll
@@ -473,6 +474,9 @@ __global__ void __launch_bounds__(reg_threads(N, CPT, Dt<T>::kVec, true), 1)
   const unsigned char* gb = reinterpret_cast<const unsigned char*>(gin);
   const int st_bytes = c.stats_stride * 4;
 
+  // Launched as a programmatic dependent of the forward: its inputs are
+  // read only after that kernel has completed.
+  pdl_wait();
   // w's loads go out before the ring fill (issued after it, they would wait
   // behind the bulk copies); they are first needed in phase B.
   bool cv[CPT];
@@ -696,11 +700,11 @@ cudaError_t launch_reg_bwd_n(const TileCfg& c, int grid, int cpt, const void* v,
   const T* gp = static_cast<const T*>(g);
   T* dvp = static_cast<T*>(dv);
   if (cpt == 1)
-    return launch_smem(reg_bwd_kernel<T, N, 1>, grid, block, smem, st, vp, w, w_dtype, gp, stats,
+    return launch_smem_pdl(reg_bwd_kernel<T, N, 1>, grid, block, smem, st, vp, w, w_dtype, gp, stats,
                        dvp, dwp, c);
   if constexpr (N <= kRegMaxN2)
     if (cpt == 2)
-      return launch_smem(reg_bwd_kernel<T, N, 2>, grid, block, smem, st, vp, w, w_dtype, gp, stats,
+      return launch_smem_pdl(reg_bwd_kernel<T, N, 2>, grid, block, smem, st, vp, w, w_dtype, gp, stats,
                          dvp, dwp, c);
   return cudaErrorInvalidValue;
 }

@@ -152,6 +152,7 @@ __global__ void __launch_bounds__(stream_threads(CPL), 1)
     }
   };
   for (int s = 0; s < c.ring && issued < nrows; ++s) issue_next(s);
+  pdl_trigger();
 
   // Lane-chunk k of a row is chunk lane + 32k; past the row end (only when
   // !FULL) it reads the zero pad instead.
@@ -361,6 +362,7 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
     }
   };
   for (int s = 0; s < c.ring; ++s) issue_next(s);
+  pdl_trigger();  // every CTA is resident: the next kernel may queue for the SMs
   if (wtma && !mbar_wait(wbar, 0u)) return;
 
   auto cval = [&](int k) { return FULL || lane + 32 * k < RC; };
@@ -570,6 +572,7 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
   };
   if (wk == 0 && lane == 0)
     for (int s = 0; s < c.ring; ++s) issue_row(s, s);
+  pdl_trigger();
   if (wtma && !mbar_wait(wbar, 0u)) return;
 
   const int cb = wk * 256 + lane;  // this lane's chunks: cb + 32k

@@ -115,6 +115,7 @@ __global__ void __launch_bounds__(kStreamBwdThreads, 1)
     mbar_fence_init();
   }
   for (int i = tid; i < streams * c.ring; i += blockDim.x) cnt0[i] = 0;
+  pdl_wait();  // a programmatic dependent of the forward: inputs after it completes
   for (int d = tid; d < c.D; d += blockDim.x) {
     const int ch = d / VEC, e = d - ch * VEC;
     wsm[((e >> 2) * RC + ch) * 4 + (e & 3)] = load_any(w, w_dtype, d);
