@@ -18,8 +18,12 @@ CPU baseline, the end-to-end number through the public API with host buffers,
 and the SM clocks sampled (NVML) during the timed region.
 
 ``--gpus N`` (under torchrun): each rank runs the same shape on its own token
-shard (weak scaling); the step's only exchange is the fp32 dw all-gather of
-``switchyard.sharding`` (NCCL).
+shard (weak scaling); the step's only exchange is the fp32 dw sum of
+``switchyard.sharding``: peer-memory copies added in rank order by one kernel
+(``sy_dw_exchange``), no NCCL on the step.
+
+``--sweep``: forward, backward and step times for bf16, fp16 and fp32 at a few
+shapes (one JSON line each; no bench line).
 
 ``--impl reference``: the reference's PyTorch eager CPU path (restated in
 ``oracle/eager_port.py``; the reference itself cannot run on the GPU box),
@@ -71,6 +75,9 @@ def parse_args():
                          "shape, for an ncu capture; prints nothing")
     ap.add_argument("--shape", default=None,
                     help="N,B,T,D for --profile (default: the representative shape)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="no bench line: time forward, backward and the fwd+bwd step through the "
+                         "C ABI for bf16, fp16 and fp32 at a few shapes, one JSON line each")
     return ap.parse_args()
 
 
@@ -512,10 +519,10 @@ def run_ours(args):
         print(json.dumps(result), flush=True)
 
 
-def kernel_label(native, op: str, n: int, bt: int, d: int) -> str:
+def kernel_label(native, op: str, n: int, bt: int, d: int, dtype=torch.bfloat16) -> str:
     """Name of the kernel the C ABI plans for this shape (sy_plan_info)."""
     code = {"fwd": 0, "bwd": 1}[op]
-    info = native.plan_info(code, n, bt, d, 1, torch.bfloat16)
+    info = native.plan_info(code, n, bt, d, 1, dtype)
     kind = info["kind"]
     if kind == 3:
         streams = info["grid"] * info["groups"]
@@ -606,6 +613,55 @@ def run_reference(args):
     }), flush=True)
 
 
+SWEEP_SHAPES = [(9, 1, 4096, 2048), (9, 1, 32768, 2048), (4, 2, 4096, 2048), (9, 1, 4096, 1024),
+                (9, 1, 4096, 4096), (17, 1, 4096, 2048), (9, 1, 4096, 8192)]
+
+
+def run_sweep(args):
+    """Forward, backward and fwd+bwd step (forward, backward, dw reduction as
+    one step, timed like the bench's kernels: clean L2, CUDA events) for each
+    dtype at each of SWEEP_SHAPES; TB/s of the algorithmic bytes and the
+    fraction of the measured copy peak. Synthetic inputs as the bench's."""
+    from switchyard import _native
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    flush = L2Flush(dev)
+    peak = load_peak_field("hbm_gbs")
+    steps = min(args.steps, 30)
+    for shape in SWEEP_SHAPES:
+        n, b, t, d = shape
+        bt = b * t
+        for dt in (torch.bfloat16, torch.float16, torch.float32):
+            v, w, dout = make_inputs(dev, 0, n, b, t, d, dtype=dt)
+            res, p = kernel_times(_native, v, w, dout, steps, flush, None)
+            out = torch.empty(b, t, d, device=dev, dtype=dt)
+            stats = torch.empty(bt, _native.stats_stride(n), device=dev, dtype=torch.float32)
+            dv = torch.empty_like(v)
+            part = torch.empty(p, d, device=dev, dtype=torch.float32)
+            dw = torch.empty(d, device=dev, dtype=dt)
+
+            def step():
+                _native.fwd(v, w, out, stats, n, bt, d, 1e-6)
+                _native.bwd(v, w, dout, stats, dv, part, n, bt, d, 1e-6)
+                _native.dw_reduce(part, dw)
+
+            for _ in range(3):
+                step()
+            st = summarize(timed_steps(step, steps, flush))
+            fb, bb, tot = alg_bytes(n, b, t, d, dt.itemsize)
+            line = {"shape": {"N": n, "B": b, "T": t, "D": d}, "dtype": str(dt).replace("torch.", ""),
+                    "fwd_kernel": kernel_label(_native, "fwd", n, bt, d, dt),
+                    "bwd_kernel": kernel_label(_native, "bwd", n, bt, d, dt)}
+            for name, byts, ms in (("fwd", fb, res["fwd"]["median_ms"]), ("bwd", bb, res["bwd"]["median_ms"]),
+                                   ("step", tot, st["median_ms"])):
+                line[name] = {"us": round(ms * 1e3, 1), "tbps": round(byts / ms / 1e9, 3),
+                              "frac_of_peak": round(byts / ms / 1e6 / peak, 3) if peak else None}
+            print(json.dumps(line), flush=True)
+            del v, dout, dv, out, part
+            torch.cuda.empty_cache()
+
+
 def run_profile(kind: str, shape: str | None = None):
     """A handful of launches at the representative shape (or `shape`,
     "N,B,T,D") and nothing else, so that an ncu capture ends by itself in
@@ -646,6 +702,9 @@ def main():
     args = parse_args()
     if args.profile:
         run_profile(args.profile, args.shape)
+        return
+    if args.sweep:
+        run_sweep(args)
         return
     if args.impl == "reference":
         run_reference(args)
