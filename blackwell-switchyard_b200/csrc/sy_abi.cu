@@ -673,6 +673,19 @@ int sy_dw_reduce(const float* dw_partial, int64_t P, int64_t D, void* dw, int dw
   return cuda_status(e, "sy_dw_reduce: launch");
 }
 
+int sy_dw_reduce_gain(const float* dw_partial, int64_t P, int64_t D, const void* w, const void* g,
+                      void* dw, void* dg, int wg_dtype, sy_stream_t stream) {
+  if (!esize_of(wg_dtype)) return SY_ERR_DTYPE;
+  if (P < 1 || D < 0) return SY_ERR_ARG;
+  if (D == 0 || (!dw && !dg)) return SY_OK;
+  if (!dw_partial || !w || !g) return SY_ERR_ARG;
+  if (D > kMaxD) return SY_ERR_UNSUPPORTED;
+  const cudaError_t e =
+      launch_dw_reduce(dw_partial, P, D, dw, wg_dtype, SY_TUNE_PDL != 0,
+                       static_cast<cudaStream_t>(stream), w, g, dg);
+  return cuda_status(e, "sy_dw_reduce_gain: launch");
+}
+
 int sy_fwd_batched(const void* v, const void* queries, void* out, int64_t N, int64_t BT, int64_t D,
                    int64_t S, int dtype, float eps, sy_stream_t stream) {
   if (!esize_of(dtype)) return SY_ERR_DTYPE;

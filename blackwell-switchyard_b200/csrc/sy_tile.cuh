@@ -108,8 +108,10 @@ cudaError_t launch_generic_bwd(long long BT, int N, int D, int dtype, const void
 cudaError_t launch_generic_batched(long long BT, int N, int D, int S, int dtype, const void* v,
                                    const void* q, void* out, float eps, int grid, cudaStream_t st);
 
-// Fixed-order column reduction of dw partials (sy_tile_bwd.cu).
+// Fixed-order column reduction of dw partials (sy_tile_bwd.cu); with gw and gg
+// (w and g of q = w * g) the result is split into dw = dq * g and dg = dq * w.
 cudaError_t launch_dw_reduce(const float* part, long long P, long long D, void* dw, int dw_dtype,
-                             bool pdl, cudaStream_t st);
+                             bool pdl, cudaStream_t st, const void* gw = nullptr,
+                             const void* gg = nullptr, void* dg = nullptr);
 
 }  // namespace sy

@@ -294,10 +294,28 @@ cudaError_t launch_tile_bwd(const TileCfg& c, int grid, int cpt, int dtype, cons
 // sums rows p = k, k+8, k+16, ... in increasing order (loaded 32 at a time),
 // then warp 0 adds the 8 warp sums in warp order. Fixed order everywhere =>
 // deterministic.
+// With a gain (gw, gg non-null) the sum is the gradient of q = w * g: it is
+// rounded to dw_dtype (as the plain reduction stores it) and split into
+// dw = dq * g and dg = dq * w, each rounded to dw_dtype -- the products and
+// roundings of the two elementwise autograd kernels it replaces. dw or dg
+// may be null (no gradient wanted).
 // ---------------------------------------------------------------------------
+__device__ __forceinline__ float round_as(int dtype, float x) {
+  switch (dtype) {
+    case SY_BF16:
+      return __bfloat162float(__float2bfloat16_rn(x));
+    case SY_F16:
+      return __half2float(__float2half_rn(x));
+    default:
+      return x;
+  }
+}
+
 __global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict__ part, long long P,
                                                         long long D, void* __restrict__ dw,
-                                                        int dw_dtype) {
+                                                        int dw_dtype, const void* __restrict__ gw,
+                                                        const void* __restrict__ gg,
+                                                        void* __restrict__ dg) {
   __shared__ float slice[8][33];
   asm volatile("griddepcontrol.wait;" ::: "memory");
   const int lane = threadIdx.x & 31;
@@ -324,12 +342,18 @@ __global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict_
     float t = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) t += slice[i][lane];
-    store_any(dw, dw_dtype, col, t);
+    if (gg == nullptr) {
+      store_any(dw, dw_dtype, col, t);
+    } else {
+      const float dq = round_as(dw_dtype, t);
+      if (dw) store_any(dw, dw_dtype, col, dq * load_any(gg, dw_dtype, col));
+      if (dg) store_any(dg, dw_dtype, col, dq * load_any(gw, dw_dtype, col));
+    }
   }
 }
 
 cudaError_t launch_dw_reduce(const float* part, long long P, long long D, void* dw, int dw_dtype,
-                             bool pdl, cudaStream_t st) {
+                             bool pdl, cudaStream_t st, const void* gw, const void* gg, void* dg) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)((D + 31) / 32));
   cfg.blockDim = dim3(256);
@@ -340,7 +364,7 @@ cudaError_t launch_dw_reduce(const float* part, long long P, long long D, void* 
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, dw_reduce_kernel, part, P, D, dw, dw_dtype);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, dw_reduce_kernel, part, P, D, dw, dw_dtype, gw, gg, dg);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -36,6 +36,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sy_bwd_partials": ([_I64, _I64, _I64, _I], _I64),
     "sy_bwd": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I, _I, _F, _P], _I),
     "sy_dw_reduce": ([_P, _I64, _I64, _P, _I, _P], _I),
+    "sy_dw_reduce_gain": ([_P, _I64, _I64, _P, _P, _P, _P, _I, _P], _I),
     "sy_fwd_batched": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I, _F, _P], _I),
     "sy_speed_of_light": ([_P, _P, _I64, _I64, _I64, _I, _P], _I),
     "sy_plan_kind": ([_I, _I64, _I64, _I64, _I64, _I], _I),
@@ -137,6 +138,19 @@ def dw_reduce(dw_partial, dw) -> None:
         lib.sy_dw_reduce(dw_partial.data_ptr(), p, d, dw.data_ptr(), dtype_code(dw.dtype),
                          stream_of(dw)),
         "sy_dw_reduce",
+    )
+
+
+def dw_reduce_gain(dw_partial, w, g, dw, dg) -> None:
+    """dq = sum of the partial rows, then dw = dq * g and dg = dq * w (either
+    output may be None)."""
+    p, d = dw_partial.shape
+    check(
+        lib.sy_dw_reduce_gain(dw_partial.data_ptr(), p, d, w.data_ptr(), g.data_ptr(),
+                              dw.data_ptr() if dw is not None else None,
+                              dg.data_ptr() if dg is not None else None,
+                              dtype_code(w.dtype), stream_of(w)),
+        "sy_dw_reduce_gain",
     )
 
 

@@ -103,23 +103,33 @@ def _forward(v: torch.Tensor, w: torch.Tensor, eps: float):
     return v, w, out, stats, strategy
 
 
+def _backward_partials(v, w, stats, grad_out, eps: float):
+    """Launch the backward. Returns ``(dv, dw_partial)``: the fp32 partial
+    rows of dw, one per CTA (None when D == 0)."""
+    n, b, t, d = v.shape
+    bt = b * t
+    g = grad_out.to(v.dtype).contiguous()
+    dv = torch.empty_like(v)
+    if d == 0:
+        return dv, None
+    with torch.cuda.device(v.device):
+        p = _native.bwd_partials(n, bt, d, v.dtype)
+        part = torch.empty(p, d, device=v.device, dtype=torch.float32)
+        _native.bwd(v, w, g, stats, dv, part, n, bt, d, eps)
+    return dv, part
+
+
 def _backward(v, w, stats, grad_out, eps: float, dw_dtype: torch.dtype, dw_out=None):
     """Launch the backward and the fixed-order dw reduction. Returns
     ``(dv, dw)`` with ``dw`` in ``dw_dtype`` (float32 for the sharded path,
     which still has to add the other ranks' contributions), written into
     ``dw_out`` when one is given."""
-    n, b, t, d = v.shape
-    bt = b * t
-    g = grad_out.to(v.dtype).contiguous()
-    dv = torch.empty_like(v)
+    d = v.shape[-1]
+    dv, part = _backward_partials(v, w, stats, grad_out, eps)
     dw = torch.empty(d, device=v.device, dtype=dw_dtype) if dw_out is None else dw_out
-    if d == 0:
-        return dv, dw
-    with torch.cuda.device(v.device):
-        p = _native.bwd_partials(n, bt, d, v.dtype)
-        part = torch.empty(p, d, device=v.device, dtype=torch.float32)
-        _native.bwd(v, w, g, stats, dv, part, n, bt, d, eps)
-        _native.dw_reduce(part, dw)
+    if part is not None:
+        with torch.cuda.device(v.device):
+            _native.dw_reduce(part, dw)
     return dv, dw
 
 
@@ -131,19 +141,40 @@ class _BlockAttnResTriton(torch.autograd.Function):
     """
 
     @staticmethod
-    def forward(ctx, v: torch.Tensor, w: torch.Tensor, eps: float):
-        _validate(v, w)
-        v, w, out, stats, strategy = _forward(v, w, eps)
-        ctx.save_for_backward(v, w, stats)
+    def forward(ctx, v: torch.Tensor, w: torch.Tensor, eps: float, gain=None):
+        # With the module's gain the query is q = w * gain (one elementwise
+        # kernel, as the reference computes it) and the backward's dw
+        # reduction also splits dq into dw = dq * gain and dgain = dq * w
+        # (sy_dw_reduce_gain) instead of leaving two products to autograd.
+        q = w if gain is None else (w * gain).contiguous()
+        _validate(v, q)
+        v, q, out, stats, strategy = _forward(v, q, eps)
+        if gain is None:
+            ctx.save_for_backward(v, q, stats)
+        else:
+            ctx.save_for_backward(v, q, stats, w.contiguous(), gain.contiguous())
+        ctx.gain = gain is not None
         ctx.eps = eps
         ctx.strategy = strategy
         return out
 
     @staticmethod
     def backward(ctx, grad_out):
-        v, w, stats = ctx.saved_tensors
-        dv, dw = _backward(v, w, stats, grad_out, ctx.eps, w.dtype)
-        return dv, dw, None
+        if not ctx.gain:
+            v, w, stats = ctx.saved_tensors
+            dv, dw = _backward(v, w, stats, grad_out, ctx.eps, w.dtype)
+            return dv, dw, None, None
+        v, q, stats, w, gain = ctx.saved_tensors
+        dv, part = _backward_partials(v, q, stats, grad_out, ctx.eps)
+        dw = torch.empty_like(w) if ctx.needs_input_grad[1] else None
+        dg = torch.empty_like(gain) if ctx.needs_input_grad[3] else None
+        if part is None:
+            dw = torch.zeros_like(w) if dw is not None else None
+            dg = torch.zeros_like(gain) if dg is not None else None
+        elif dw is not None or dg is not None:
+            with torch.cuda.device(v.device):
+                _native.dw_reduce_gain(part, w, gain, dw, dg)
+        return dv, dw, None, dg
 
 
 def block_attn_res_triton(v: torch.Tensor, w: torch.Tensor, eps: float = DEFAULT_EPS):
@@ -225,5 +256,9 @@ class BlockAttnResTriton(torch.nn.Module):
         return f"d_model={self.d_model}, norm_affine={self.g is not None}, eps={self.eps}"
 
     def forward(self, v: torch.Tensor) -> torch.Tensor:
-        q = self.w if self.g is None else self.w * self.g
-        return block_attn_res_triton(v, q, self.eps)
+        if self.g is None:
+            return block_attn_res_triton(v, self.w, self.eps)
+        if self.w.dtype == self.g.dtype and self.w.device == self.g.device:
+            # q = w * g, with dq split into dw and dg inside the dw reduction
+            return _BlockAttnResTriton.apply(v, self.w, self.eps, self.g)
+        return block_attn_res_triton(v, self.w * self.g, self.eps)

@@ -112,6 +112,18 @@ SY_API int sy_dw_reduce(const float* dw_partial, int64_t P, int64_t D, void* dw,
                  int dw_dtype, sy_stream_t stream);
 
 /*
+ * sy_dw_reduce with the module's gain folded in. BlockAttnResTriton's forward
+ * queries with q = w * g (src/switchyard/triton_op.py:605-609), so autograd
+ * turns the reduced dq into dw = dq * g and dg = dq * w with two more
+ * elementwise kernels; this call does the reduction and both products in one
+ * launch, with the same roundings (dq rounded to wg_dtype first, each product
+ * rounded to wg_dtype). w, g, dw, dg: [D] of wg_dtype; dw or dg may be NULL
+ * (that gradient is not written).
+ */
+SY_API int sy_dw_reduce_gain(const float* dw_partial, int64_t P, int64_t D, const void* w,
+                      const void* g, void* dw, void* dg, int wg_dtype, sy_stream_t stream);
+
+/*
  * Batched-query forward, output only: out[s] = forward(v, queries[s]).
  * Replaces block_attn_res_batched and _fwd_batched_resident
  * (src/switchyard/triton_op.py:438-501, :378-414), including the shapes the

@@ -31,7 +31,8 @@ def native():
 
 def test_header_declares_the_entry_points():
     names = _declared()
-    for required in ("sy_fwd", "sy_bwd", "sy_bwd_partials", "sy_dw_reduce", "sy_fwd_batched",
+    for required in ("sy_fwd", "sy_bwd", "sy_bwd_partials", "sy_dw_reduce", "sy_dw_reduce_gain",
+                     "sy_fwd_batched",
                      "sy_speed_of_light", "sy_stats_stride", "sy_status_string"):
         assert required in names
 
@@ -88,6 +89,12 @@ def test_host_validation_rejects_bad_arguments(native):
     assert L.sy_dw_exchange(1, 0, 0, 0, 64, 1, 8, 1, bf16, None) == native.SY_ERR_ARG
     assert L.sy_dw_exchange(1, 2, 0, 0, 64, 1, 8, 1, bad, None) == native.SY_ERR_DTYPE
     assert L.sy_dw_exchange(None, 2, 0, 0, 64, 1, 0, None, bf16, None) == native.SY_OK
+    # gain-split dw reduction: dtype, null inputs, nothing to write, empty D
+    assert L.sy_dw_reduce_gain(1, 4, 8, 1, 1, 1, 1, bad, None) == native.SY_ERR_DTYPE
+    assert L.sy_dw_reduce_gain(1, 4, 8, None, 1, 1, 1, bf16, None) == native.SY_ERR_ARG
+    assert L.sy_dw_reduce_gain(1, 0, 8, 1, 1, 1, 1, bf16, None) == native.SY_ERR_ARG
+    assert L.sy_dw_reduce_gain(1, 4, 8, 1, 1, None, None, bf16, None) == native.SY_OK
+    assert L.sy_dw_reduce_gain(None, 4, 0, None, None, 1, 1, bf16, None) == native.SY_OK
 
 
 B200 = dict(sms=148, max_smem=232448)  # multiprocessors, opt-in shared memory per block

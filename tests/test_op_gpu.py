@@ -99,6 +99,34 @@ def test_module_matches_functional():
     torch.testing.assert_close(m(v), block_attn_res_triton(v, m.w * m.g, m.eps))
 
 
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("which", ["both", "w", "g"])
+def test_module_gain_split_matches_autograd_bitwise(dtype, which):
+    """The module folds dq -> (dw = dq * g, dg = dq * w) into the dw reduction
+    (sy_dw_reduce_gain); autograd through w * g gives the same bits."""
+    m = BlockAttnResTriton(2048).to(DEV).to(dtype)
+    with torch.no_grad():
+        m.w.copy_(randn(2048, seed=31) / 2048**0.5)
+        m.g.copy_(1 + 0.1 * randn(2048, seed=32))
+    m.w.requires_grad_(which in ("both", "w"))
+    m.g.requires_grad_(which in ("both", "g"))
+    v = randn(9, 1, 300, 2048, dtype=torch.bfloat16, seed=33).requires_grad_(True)
+    gout = randn(1, 300, 2048, dtype=torch.bfloat16, seed=34)
+    out = m(v)
+    out.backward(gout)
+    w2 = m.w.detach().clone().requires_grad_(m.w.requires_grad)
+    g2 = m.g.detach().clone().requires_grad_(m.g.requires_grad)
+    v2 = v.detach().clone().requires_grad_(True)
+    out2 = block_attn_res_triton(v2, w2 * g2, m.eps)
+    out2.backward(gout)
+    assert torch.equal(out, out2) and torch.equal(v.grad, v2.grad)
+    for p1, p2 in ((m.w, w2), (m.g, g2)):
+        if p1.requires_grad:
+            assert p1.grad.dtype == dtype and torch.equal(p1.grad, p2.grad)
+        else:
+            assert p1.grad is None
+
+
 def test_module_starts_from_uniform_attention():
     m = BlockAttnResTriton(128).to(DEV)
     v = randn(7, 1, 32, 128)
