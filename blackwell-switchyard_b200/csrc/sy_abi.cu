@@ -34,6 +34,9 @@
 #ifndef SY_TUNE_STREAM_BWD
 #define SY_TUNE_STREAM_BWD 1  // backward: row stream before the shared-memory tile
 #endif
+#ifndef SY_TUNE_REREAD_CPL4
+#define SY_TUNE_REREAD_CPL4 1  // forward, 2 KiB rows: re-read row stream (4 chunks per lane)
+#endif
 #ifndef SY_TUNE_BATCHED_REG
 #define SY_TUNE_BATCHED_REG 1  // batched: the register tile where it fits (else row stream)
 #endif
@@ -246,9 +249,10 @@ StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInf
   if (!es || N < 1 || D < 1 || D > kMaxD || BT < 1 || BT > INT_MAX) return p;
   if ((D * es) % 16) return p;
   const int64_t rc = D * es / 16;
-  // Rows of exactly 2 or 4 times 4 KiB: the split re-read kernel, K warps per
-  // token. Otherwise one warp per token, rows of at most 8 chunks per lane.
-  const int kw = (!sol && SY_TUNE_STREAM_REREAD && (rc == 512 || rc == 1024)) ? (int)(rc / 256) : 1;
+  // Rows of exactly 2, 4 or 8 times 4 KiB: the split re-read kernel, K warps
+  // per token. Otherwise one warp per token, rows of at most 8 chunks per lane.
+  const int kw =
+      (!sol && SY_TUNE_STREAM_REREAD && (rc == 512 || rc == 1024 || rc == 2048)) ? (int)(rc / 256) : 1;
   int cpl = 1;
   while (cpl * 32 * kw < rc) cpl *= 2;
   if (cpl > 8) return p;
@@ -259,7 +263,13 @@ StreamPlan plan_stream(int64_t N, int64_t BT, int64_t D, int dtype, const DevInf
   c.row_chunks = (int)rc;
   c.row_bytes = (int)(D * es);
   c.kw = kw;
-  c.reread = (SY_TUNE_STREAM_REREAD && cpl == 8 && !sol) ? 1 : 0;
+  // 2 KiB rows: the re-read stream where the register tile's stage-held
+  // forward does not apply (N > 9, or fewer than kHoldMinTokensPerSM tokens
+  // per SM); that one is faster from there on (5.95 vs 4.96 TB/s at N=9
+  // T=32768 D=1024 bf16).
+  const bool cpl4 = cpl == 4 && kw == 1 && SY_TUNE_REREAD_CPL4 &&
+                    (N > kRegFwdMaxN || BT < (int64_t)kHoldMinTokensPerSM * di.sms);
+  c.reread = (SY_TUNE_STREAM_REREAD && !sol && (cpl == 8 || cpl4)) ? 1 : 0;
   c.warps = stream_threads(cpl, c.reread != 0) / 32;
   if (c.reread) {
     // Whole tokens per token stream (a warp, or K warps), as even as possible:

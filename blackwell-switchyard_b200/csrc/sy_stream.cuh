@@ -287,7 +287,8 @@ __device__ __forceinline__ void stage_w(float* wsm, const void* w, int w_dtype, 
   }
 }
 
-// Re-read variant of the row stream (8 chunks per lane: 4 KiB rows). Per row,
+// Re-read variant of the row stream (8 chunks per lane: 4 KiB rows, or 4: 2 KiB
+// rows). Per row,
 // pass 1 reads the lane's chunks from the row buffer for the dot and the sum
 // of squares only; after the online-softmax update pass 2 reads them again
 // for o (o += p * v_n; a new maximum first rescales o and enters v_n with
@@ -296,11 +297,11 @@ __device__ __forceinline__ void stage_w(float* wsm, const void* w, int w_dtype, 
 // counters and one running source pointer, so 14 warps (128 registers) fit
 // on an SM: with whole tokens per warp that balances 28 tokens per SM as
 // 2 per warp (the representative 4096 tokens on 148 SMs).
-template <typename T, bool FULL, bool MIX>
+template <typename T, int CPL, bool FULL, bool MIX>
 __global__ void __launch_bounds__(kStreamRereadThreads, 1)
     stream_fwd_reread_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
                              T* __restrict__ out, float* __restrict__ stats, const StreamCfg c) {
-  constexpr int CPL = 8;
+  static_assert(CPL == 4 || CPL == 8, "4 or 8 chunks per lane");
   constexpr int VEC = Dt<T>::kVec;
   constexpr int P = VEC / 2;
   const int RC = FULL ? 32 * CPL : c.row_chunks;  // chunks per row
@@ -433,7 +434,7 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
                                         __shfl_xor_sync(kFull, ds.y, off)));
       const float r = rsqrtf(ds.y * inv_d + c.eps);
       const float logit = ds.x * r;
-      if (lane == (n & 31)) {
+      if (lane == n) {  // (never for n >= 32: those rows are written directly below)
         lane_logit = logit;
         lane_r = r;
       }
@@ -503,8 +504,8 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
   }
 }
 
-// Split variant of the re-read row stream for rows of K * 4 KiB (K = 2, 4: D =
-// 4096 / 8192 bf16): K warps share each token, warp k taking chunks
+// Split variant of the re-read row stream for rows of K * 4 KiB (K = 2, 4, 8: D =
+// 4096 / 8192 / 16384 bf16): K warps share each token, warp k taking chunks
 // 256k .. 256k+255 of every row (8 per lane). Per row each warp reduces its
 // part of (dot, ssq) over its lanes; lane 0 publishes the pair, the K warps
 // meet at a named barrier and every warp adds the K pairs in warp order, so all
@@ -646,7 +647,7 @@ __global__ void __launch_bounds__(kStreamRereadThreads, 1)
       for (int k2 = 1; k2 < K; ++k2) ds = __fadd2_rn(ds, xr[k2]);
       const float r = rsqrtf(ds.y * inv_d + c.eps);
       const float logit = ds.x * r;
-      if (lane == (n & 31)) {
+      if (lane == n) {  // (never for n >= 32: those rows are written directly below)
         lane_logit = logit;
         lane_r = r;
       }
@@ -726,18 +727,25 @@ cudaError_t launch_stream_fwd(const StreamCfg& c, int grid, int cpl, int dtype, 
 #endif
 
 template <typename T, bool FULL, bool MIX>
-cudaError_t launch_stream_reread(const StreamCfg& c, int grid, dim3 block, size_t smem,
+cudaError_t launch_stream_reread(const StreamCfg& c, int grid, int cpl, dim3 block, size_t smem,
                                  const T* vp, const void* w, int w_dtype, T* op, float* stats,
                                  cudaStream_t st) {
-  if (c.kw <= 1)
-    return launch_smem(stream_fwd_reread_kernel<T, FULL, MIX>, grid, block, smem, st, vp, w,
+  if (c.kw <= 1 && cpl == 8)
+    return launch_smem(stream_fwd_reread_kernel<T, 8, FULL, MIX>, grid, block, smem, st, vp, w,
                        w_dtype, op, stats, c);
+  if (c.kw <= 1 && cpl == 4)
+    return launch_smem(stream_fwd_reread_kernel<T, 4, FULL, MIX>, grid, block, smem, st, vp, w,
+                       w_dtype, op, stats, c);
+  if (cpl != 8) return cudaErrorInvalidValue;
   if constexpr (FULL) {
     if (c.kw == 2)
       return launch_smem(stream_fwd_split_kernel<T, 2, MIX>, grid, block, smem, st, vp, w,
                          w_dtype, op, stats, c);
     if (c.kw == 4)
       return launch_smem(stream_fwd_split_kernel<T, 4, MIX>, grid, block, smem, st, vp, w,
+                         w_dtype, op, stats, c);
+    if (c.kw == 8)
+      return launch_smem(stream_fwd_split_kernel<T, 8, MIX>, grid, block, smem, st, vp, w,
                          w_dtype, op, stats, c);
   }
   return cudaErrorInvalidValue;
@@ -752,14 +760,14 @@ cudaError_t launch_stream_tf(const StreamCfg& c, int grid, int cpl, const void* 
   T* op = static_cast<T*>(out);
   if (c.reread) {
     if constexpr (!SOL) {
-      if (cpl == 8 && (int)block.x <= kStreamRereadThreads) {
+      if ((cpl == 8 || cpl == 4) && (int)block.x <= kStreamRereadThreads) {
         // w of the sources' own 16-bit type: pass 1 on the packed halves
         if constexpr (sizeof(T) == 2) {
           if (w_dtype == Dt<T>::kCode && SY_TUNE_FWD_MIX)
-            return launch_stream_reread<T, FULL, true>(c, grid, block, smem, vp, w, w_dtype, op,
-                                                       stats, st);
+            return launch_stream_reread<T, FULL, true>(c, grid, cpl, block, smem, vp, w, w_dtype,
+                                                       op, stats, st);
         }
-        return launch_stream_reread<T, FULL, false>(c, grid, block, smem, vp, w, w_dtype, op,
+        return launch_stream_reread<T, FULL, false>(c, grid, cpl, block, smem, vp, w, w_dtype, op,
                                                     stats, st);
       }
     }

@@ -133,8 +133,8 @@ def test_planner_invariants_for_b200(native, dtype_name):
                     assert n <= 64
                 if p["kind"] == 1:
                     assert n <= 16
-                if p["kind"] == 3 and op == 0:  # row-stream forward: a token per 1, 2 or 4 warps
-                    assert p["threads_per_group"] in (32, 64, 128)
+                if p["kind"] == 3 and op == 0:  # row-stream forward: a token per 1, 2, 4 or 8 warps
+                    assert p["threads_per_group"] in (32, 64, 128, 256)
                     assert p["chunks_per_thread"] * p["threads_per_group"] * 16 >= d * dt.itemsize
                     assert p["groups"] * p["threads_per_group"] <= 512 and p["stages"] >= 2
                 if p["kind"] == 3 and op == 1:  # row-stream backward: 4 chunks per lane, exact
@@ -149,8 +149,11 @@ def test_planner_invariants_for_b200(native, dtype_name):
     assert rep["grid"] * rep["groups"] * 2 >= 4096
     assert native.plan_info(0, 17, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 3
     assert native.plan_info(0, 9, 4096, 512, 1, torch.bfloat16, **B200)["kind"] == 1
-    # 8 and 16 KiB rows: the split row stream, 2 and 4 warps per token
-    for d, kw in ((4096, 2), (8192, 4)):
+    # 2 KiB rows: the re-read row stream with 4 chunks per lane
+    p = native.plan_info(0, 9, 4096, 1024, 1, torch.bfloat16, **B200)
+    assert p["kind"] == 3 and p["chunks_per_thread"] == 4 and p["threads_per_group"] == 32
+    # 8, 16 and 32 KiB rows: the split row stream, 2, 4 and 8 warps per token
+    for d, kw in ((4096, 2), (8192, 4), (16384, 8)):
         p = native.plan_info(0, 9, 4096, d, 1, torch.bfloat16, **B200)
         assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw and p["stages"] >= 3
     assert native.plan_info(1, 9, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 1

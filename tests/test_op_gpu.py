@@ -213,7 +213,8 @@ def test_dispatch_sends_the_representative_shape_to_the_tile_kernels():
 
 EPS_SHAPES = [  # fp32 shapes that reach every kernel family
     ((9, 1, 64, 1024), PLAN_STREAM, PLAN_TILE),  # 4 KiB rows: re-read row stream
-    ((7, 2, 16, 512), PLAN_TILE, PLAN_TILE),
+    ((7, 2, 16, 512), PLAN_STREAM, PLAN_TILE),  # 2 KiB rows: re-read row stream, 4 chunks/lane
+    ((7, 2, 16, 256), PLAN_TILE, PLAN_TILE),
     ((9, 1, 48, 256), PLAN_TILE, PLAN_TILE),
     ((17, 1, 40, 1024), PLAN_STREAM, PLAN_STREAM),  # backward: 2 warps per token
     ((10, 1, 24, 2048), PLAN_STREAM, PLAN_STREAM),  # 8 KiB rows: split row streams
@@ -362,7 +363,7 @@ def test_representative_shape_full_size_properties():
 
 
 @pytest.mark.parametrize("shape", [(9, 1, 600, 2048), (9, 1, 300, 4096), (9, 1, 150, 8192),
-                                   (4, 2, 100, 1800)])
+                                   (3, 1, 60, 16384), (9, 1, 600, 1024), (4, 2, 100, 1800)])
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_forward_same_bits_for_16bit_and_fp32_queries(shape, dtype):
     """A query of the sources' own 16-bit type takes the packed mixed-precision
@@ -380,6 +381,24 @@ def test_forward_same_bits_for_16bit_and_fp32_queries(shape, dtype):
     _native.fwd(v, w, o[0], stats[0], n, b * t, d, DEFAULT_EPS)
     _native.fwd(v, w.float(), o[1], stats[1], n, b * t, d, DEFAULT_EPS)
     assert torch.equal(o[0], o[1]) and torch.equal(stats[0], stats[1])
+
+
+@pytest.mark.parametrize("shape", [(40, 1, 64, 2048), (36, 1, 48, 1024), (40, 1, 24, 4096)])
+def test_statistics_of_more_than_32_sources(shape):
+    """The row-stream forwards keep row n's statistics in lane n for n < 32 and
+    write later rows directly; the backward reads them back (re-read stream at
+    4 and 2 KiB rows, split stream at 8 KiB rows)."""
+    n, b, t, d = shape
+    assert _plan("fwd", n, b * t, d, torch.bfloat16) == PLAN_STREAM
+    v = randn(*shape, dtype=torch.bfloat16, seed=41)
+    w = randn(d, dtype=torch.bfloat16, seed=42, scale=d ** -0.5)
+    g = randn(b, t, d, dtype=torch.bfloat16, seed=43)
+    out, dv, dw = fwd_bwd(v, w, g)
+    o_ref = O.forward(np64(v), np64(w))
+    dv_ref, dw_ref = O.backward(np64(v), np64(w), np64(g))
+    assert O.rel_l2(np64(out), o_ref) <= 1.005 * O.dtype_floor(o_ref, "bfloat16")
+    assert O.rel_l2(np64(dv), dv_ref) <= 1.005 * O.dtype_floor(dv_ref, "bfloat16")
+    assert O.rel_l2(np64(dw), dw_ref) <= 1.005 * O.dtype_floor(dw_ref, "bfloat16")
 
 
 @pytest.mark.parametrize("shape,dtype", [
