@@ -88,6 +88,7 @@ int esize_of(int dtype) {
 }
 
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+bool al8(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 7u) == 0; }
 
 int64_t stats_stride(int64_t N) { return ((2 * N + 2) + 3) / 4 * 4; }
 
@@ -365,7 +366,7 @@ TilePlan plan_batched(int64_t N, int64_t BT, int64_t D, int64_t S, int dtype, co
   TilePlan p;
   if (!SY_TUNE_BATCHED_REG) return p;
   const int es = esize_of(dtype);
-  if (!es || N < 1 || N > kRegMaxN || S < 2 || S > kBatchedMaxS || D < 1 || D > kMaxD ||
+  if (!es || N < 1 || N > kRegMaxN || S < 1 || S > kBatchedMaxS || D < 1 || D > kMaxD ||
       BT < 1 || BT > INT_MAX)
     return p;
   if ((D * es) % 16) return p;
@@ -417,7 +418,7 @@ StreamBatchedPlan plan_stream_batched(int64_t N, int64_t BT, int64_t D, int64_t 
                                       const DevInfo& di) {
   StreamBatchedPlan p;
   const int es = esize_of(dtype);
-  if (!es || N < 1 || N > kStreamBatchedMaxN || S < 2 || S > kStreamBatchedMaxS || D < 1 ||
+  if (!es || N < 1 || N > kStreamBatchedMaxN || S < 1 || S > kStreamBatchedMaxS || D < 1 ||
       D > kMaxD || BT < 1 || BT > INT_MAX)
     return p;
   if ((D * es) % 16) return p;
@@ -721,9 +722,94 @@ int sy_fwd_batched(const void* v, const void* queries, void* out, int64_t N, int
     return cuda_status(e, "sy_fwd_batched: stream kernel launch");
   }
   if (!generic_batched_fits(N, S, di)) return SY_ERR_UNSUPPORTED;
-  e = launch_generic_batched(BT, (int)N, (int)D, (int)S, dtype, v, queries, out, eps,
+  e = launch_generic_batched(BT, (int)N, (int)D, (int)S, dtype, nullptr, 0, v, queries, out, eps,
                              generic_grid(BT, di), static_cast<cudaStream_t>(stream));
   return cuda_status(e, "sy_fwd_batched: generic kernel launch");
+}
+
+int sy_fwd_batched_stats(const void* v, const void* queries, void* out, float* mstats, int raw,
+                         int64_t N, int64_t BT, int64_t D, int64_t S, int dtype, float eps,
+                         sy_stream_t stream) {
+  if (!esize_of(dtype)) return SY_ERR_DTYPE;
+  if (N < 1 || BT < 0 || D < 0 || S < 1 || (raw != 0 && raw != 1)) return SY_ERR_ARG;
+  if (BT == 0 || D == 0) return SY_OK;
+  if (!v || !queries || !out || !mstats) return SY_ERR_ARG;
+  if (D > kMaxD || BT > INT_MAX || S > INT_MAX) return SY_ERR_UNSUPPORTED;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  DevInfo di;
+  cudaError_t e = dev_info(&di);
+  if (e != cudaSuccess) return cuda_status(e, "sy_fwd_batched_stats: device query");
+  const bool aligned = al16(v) && al16(queries) && al16(out) && al8(mstats);
+  TilePlan bp = plan_batched(N, BT, D, S, dtype, di);
+  bp.c.eps = eps;
+  bp.c.mstats = mstats;
+  bp.c.raw = raw;
+  if (bp.kind == kPlanRegTile && aligned) {
+    e = launch_plan_batched(bp, (int)S, dtype, v, queries, out, st);
+    return cuda_status(e, "sy_fwd_batched_stats: register-tile kernel launch");
+  }
+  StreamBatchedPlan sb = plan_stream_batched(N, BT, D, S, dtype, di);
+  sb.c.eps = eps;
+  sb.c.mstats = mstats;
+  sb.c.raw = raw;
+  if (sb.ok && aligned) {
+    e = launch_stream_batched(sb.c, sb.grid, dtype, v, queries, out, st);
+    return cuda_status(e, "sy_fwd_batched_stats: stream kernel launch");
+  }
+  if (!generic_batched_fits(N, S, di) || !al8(mstats)) return SY_ERR_UNSUPPORTED;
+  e = launch_generic_batched(BT, (int)N, (int)D, (int)S, dtype, mstats, raw, v, queries, out, eps,
+                             generic_grid(BT, di), st);
+  return cuda_status(e, "sy_fwd_batched_stats: generic kernel launch");
+}
+
+int64_t sy_bwd_batched_partials(int64_t N, int64_t BT, int64_t D, int64_t S, int dtype) {
+  if (!esize_of(dtype) || N < 1 || BT < 0 || D < 0 || S < 1) return -SY_ERR_ARG;
+  if (BT == 0 || D == 0) return 1;
+  DevInfo di;
+  if (dev_info(&di) != cudaSuccess) return -SY_ERR_CUDA;
+  const int64_t g = (int64_t)di.sms * 2;
+  return BT < g ? BT : g;
+}
+
+int sy_bwd_batched(const void* v, const void* queries, const void* g, void* dv,
+                   float* dq_partial, int64_t P, int64_t N, int64_t BT, int64_t D,
+                   int64_t S, int dtype, float eps, sy_stream_t stream) {
+  if (!esize_of(dtype)) return SY_ERR_DTYPE;
+  if (N < 1 || BT < 0 || D < 0 || S < 1 || P < 1) return SY_ERR_ARG;
+  if (P != sy_bwd_batched_partials(N, BT, D, S, dtype)) return SY_ERR_ARG;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D == 0) return SY_OK;
+  if (!dq_partial) return SY_ERR_ARG;
+  if (BT == 0)
+    return cuda_status(cudaMemsetAsync(dq_partial, 0, (size_t)P * S * D * sizeof(float), st),
+                       "sy_bwd_batched: zero dq_partial");
+  if (!v || !queries || !g || !dv) return SY_ERR_ARG;
+  if (S > 16) return SY_ERR_UNSUPPORTED;
+  if (D > kMaxD || BT > INT_MAX) return SY_ERR_UNSUPPORTED;
+  DevInfo di;
+  cudaError_t e = dev_info(&di);
+  if (e != cudaSuccess) return cuda_status(e, "sy_bwd_batched: device query");
+  if (bwd_batched_smem((int)N, (int)S) > (size_t)di.max_smem) return SY_ERR_UNSUPPORTED;
+  e = launch_bwd_batched(BT, (int)N, (int)D, (int)S, dtype, v, queries, g, dv, dq_partial, (int)P,
+                         eps, st);
+  return cuda_status(e, "sy_bwd_batched: kernel launch");
+}
+
+int sy_merge_stats(const void* o1, const float* ms1, const void* o2, const float* ms2, void* o,
+                   float* ms, int normalize, int64_t R, int64_t D, int dtype,
+                   sy_stream_t stream) {
+  if (!esize_of(dtype)) return SY_ERR_DTYPE;
+  if (R < 0 || D < 0 || (normalize != 0 && normalize != 1)) return SY_ERR_ARG;
+  if (R == 0) return SY_OK;
+  if (!o1 || !ms1 || !o2 || !ms2 || (D > 0 && !o)) return SY_ERR_ARG;
+  if (!al8(ms1) || !al8(ms2) || (ms && !al8(ms))) return SY_ERR_ARG;
+  if (D > kMaxD) return SY_ERR_UNSUPPORTED;
+  DevInfo di;
+  cudaError_t e = dev_info(&di);
+  if (e != cudaSuccess) return cuda_status(e, "sy_merge_stats: device query");
+  e = launch_merge(R, (int)D, dtype, o1, ms1, o2, ms2, o, ms, normalize, generic_grid(R, di),
+                   static_cast<cudaStream_t>(stream));
+  return cuda_status(e, "sy_merge_stats: kernel launch");
 }
 
 int sy_speed_of_light(const void* v, void* out, int64_t N, int64_t BT, int64_t D, int dtype,

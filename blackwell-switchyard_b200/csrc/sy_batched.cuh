@@ -233,7 +233,9 @@ __global__ void __launch_bounds__(kBatchedThreads, 1)
       float l = 0.f;
 #pragma unroll
       for (int jj = 0; jj < N; ++jj) l += __shfl_sync(kFull, e, base + jj);
-      const float al = e / l;
+      const float al = c.raw ? e : e / l;
+      if (c.mstats != nullptr && act && n == 0)
+        reinterpret_cast<float2*>(c.mstats)[(size_t)(s0 + qi) * c.BT + tok] = make_float2(m, l);
       __syncwarp();  // the previous block's reads of the slot are done
       if (act) reinterpret_cast<float2*>(alpha_slot)[lane] = make_float2(al, al);
       __syncwarp();

@@ -167,7 +167,8 @@ __global__ void __launch_bounds__(kGenericThreads)
 template <typename T>
 __global__ void __launch_bounds__(kGenericThreads)
     gen_batched_kernel(const T* __restrict__ v, const T* __restrict__ q, T* __restrict__ out,
-                       long long BT, int N, int D, int S, float eps) {
+                       long long BT, int N, int D, int S, float eps, float* __restrict__ mstats,
+                       int raw) {
   extern __shared__ float gsm[];
   const int S1 = S + 1;
   float* part = gsm;                    // [N][S+1][kGW]   (index S = sum of squares)
@@ -208,8 +209,12 @@ __global__ void __launch_bounds__(kGenericThreads)
         l += p;
       }
       l = warp_sum(l);
-      const float inv = 1.f / l;
-      for (int n = lane; n < N; n += 32) alpha[s * N + n] *= inv;
+      if (mstats != nullptr && lane == 0)
+        reinterpret_cast<float2*>(mstats)[(size_t)s * BT + tok] = make_float2(m, l);
+      if (!raw) {
+        const float inv = 1.f / l;
+        for (int n = lane; n < N; n += 32) alpha[s * N + n] *= inv;
+      }
     }
     __syncthreads();
     for (int s = 0; s < S; ++s)
@@ -273,14 +278,14 @@ cudaError_t launch_generic_bwd(long long BT, int N, int D, int dtype, const void
                                      static_cast<T*>(dv), dw_partial, BT, N, D, eps))
 }
 
-cudaError_t launch_generic_batched(long long BT, int N, int D, int S, int dtype, const void* v,
-                                   const void* q, void* out, float eps, int grid,
-                                   cudaStream_t st) {
+cudaError_t launch_generic_batched(long long BT, int N, int D, int S, int dtype, float* mstats,
+                                   int raw, const void* v, const void* q, void* out, float eps,
+                                   int grid, cudaStream_t st) {
   const size_t smem = ((size_t)N * (S + 1) * kGW + (size_t)S * N) * sizeof(float);
   SY_DTYPE_SWITCH(dtype, T,
                   return launch_smem(gen_batched_kernel<T>, grid, kGenericThreads, smem, st,
                                      static_cast<const T*>(v), static_cast<const T*>(q),
-                                     static_cast<T*>(out), BT, N, D, S, eps))
+                                     static_cast<T*>(out), BT, N, D, S, eps, mstats, raw))
 }
 
 }  // namespace sy

@@ -39,6 +39,8 @@ struct StreamBatchedCfg {
   int warps;       // per CTA, a multiple of kw
   int ring;        // row buffers per token stream
   float eps;
+  float* mstats;   // optional (max logit, sum of exponentials) per (query, token)
+  int raw;         // 1: unnormalised output sum_n exp(logit_n - max) v_n
 };
 
 constexpr int kStreamBatchedThreads = 512;
@@ -95,7 +97,7 @@ __global__ void __launch_bounds__(kStreamBatchedThreads, 1)
   if (K < 2 || K > 16 || c.warps % K != 0 || c.warps != (int)(blockDim.x >> 5) ||
       c.warps / K > 8 || c.ring < 2 || c.cpl != CPL || c.sb != SB ||
       c.row_chunks != 32 * CPL * K || RB != 16 * c.row_chunks || N < 1 ||
-      N > kStreamBatchedMaxN || S < 2 || S > SB) {
+      N > kStreamBatchedMaxN || S < 1 || S > SB) {
     if (tid == 0) record_device_error(kDevErrBadPlan);
     return;
   }
@@ -270,7 +272,9 @@ __global__ void __launch_bounds__(kStreamBatchedThreads, 1)
       const float m = warp_max(logit);
       const float e = act ? expf(logit - m) : 0.f;
       const float l = warp_sum(e);
-      if (act) alpha[s * N + lane] = e / l;
+      if (act) alpha[s * N + lane] = c.raw ? e : e / l;
+      if (c.mstats != nullptr && lane == 0)
+        reinterpret_cast<float2*>(c.mstats)[(size_t)s * c.BT + tok] = make_float2(m, l);
     }
     named_sync(1 + gi, 32 * K);
 

@@ -42,6 +42,11 @@ struct TileCfg {
   int w_smem;        // register-tile forward: w kept in shared memory (fp32)
   int hold;          // register-tile forward: tile held in the stage (no register copy)
   float eps;
+  // batched forward only: per (query, token) (max logit, sum of exp(logit - max))
+  // as float pairs [S][BT][2] when non-null, and raw = 1 writes the
+  // unnormalised sum_n exp(logit_n - max) v_n instead of the softmax average
+  float* mstats;
+  int raw;
 };
 
 // Per-warp scratch sizes for N sources: the reduction holds 16 values per
@@ -105,7 +110,15 @@ cudaError_t launch_generic_bwd(long long BT, int N, int D, int dtype, const void
                                const void* w, int w_dtype, const void* g, const float* stats,
                                int stats_stride, void* dv, float* dw_partial, int P, float eps,
                                cudaStream_t st);
-cudaError_t launch_generic_batched(long long BT, int N, int D, int S, int dtype, const void* v,
+cudaError_t launch_bwd_batched(long long BT, int N, int D, int S, int dtype, const void* v,
+                               const void* q, const void* g, void* dv, float* dq_partial, int P,
+                               float eps, cudaStream_t st);
+size_t bwd_batched_smem(int N, int S);
+cudaError_t launch_merge(long long R, int D, int dtype, const void* o1, const float* ms1,
+                         const void* o2, const float* ms2, void* o, float* ms, int normalize,
+                         int grid, cudaStream_t st);
+cudaError_t launch_generic_batched(long long BT, int N, int D, int S, int dtype, float* mstats,
+                                   int raw, const void* v,
                                    const void* q, void* out, float eps, int grid, cudaStream_t st);
 
 // Fixed-order column reduction of dw partials (sy_tile_bwd.cu); with gw and gg

@@ -38,6 +38,10 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sy_dw_reduce": ([_P, _I64, _I64, _P, _I, _P], _I),
     "sy_dw_reduce_gain": ([_P, _I64, _I64, _P, _P, _P, _P, _I, _P], _I),
     "sy_fwd_batched": ([_P, _P, _P, _I64, _I64, _I64, _I64, _I, _F, _P], _I),
+    "sy_fwd_batched_stats": ([_P, _P, _P, _P, _I, _I64, _I64, _I64, _I64, _I, _F, _P], _I),
+    "sy_bwd_batched_partials": ([_I64, _I64, _I64, _I64, _I], _I64),
+    "sy_bwd_batched": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I, _F, _P], _I),
+    "sy_merge_stats": ([_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I, _P], _I),
     "sy_speed_of_light": ([_P, _P, _I64, _I64, _I64, _I, _P], _I),
     "sy_plan_kind": ([_I, _I64, _I64, _I64, _I64, _I], _I),
     "sy_plan_info": ([_I, _I64, _I64, _I64, _I64, _I, _I, _I, _c.POINTER(_I64)], _I),
@@ -159,6 +163,42 @@ def fwd_batched(v, q, out, n, bt, d, s, eps) -> None:
         lib.sy_fwd_batched(v.data_ptr(), q.data_ptr(), out.data_ptr(), n, bt, d, s,
                            dtype_code(v.dtype), float(eps), stream_of(v)),
         "sy_fwd_batched",
+    )
+
+
+def fwd_batched_stats(v, q, out, mstats, raw: bool, n, bt, d, s, eps) -> None:
+    """Batched forward writing (m, l) per (query, token) into ``mstats``
+    ([S, BT, 2] fp32); ``raw`` leaves the output unnormalised."""
+    check(
+        lib.sy_fwd_batched_stats(v.data_ptr(), q.data_ptr(), out.data_ptr(), mstats.data_ptr(),
+                                 1 if raw else 0, n, bt, d, s, dtype_code(v.dtype), float(eps),
+                                 stream_of(v)),
+        "sy_fwd_batched_stats",
+    )
+
+
+def bwd_batched_partials(n, bt, d, s, dtype) -> int:
+    p = int(lib.sy_bwd_batched_partials(n, bt, d, s, dtype_code(dtype)))
+    if p < 1:
+        raise NativeError("sy_bwd_batched_partials", -p)
+    return p
+
+
+def bwd_batched(v, q, g, dv, dq_partial, n, bt, d, s, eps) -> None:
+    check(
+        lib.sy_bwd_batched(v.data_ptr(), q.data_ptr(), g.data_ptr(), dv.data_ptr(),
+                           dq_partial.data_ptr(), dq_partial.shape[0], n, bt, d, s,
+                           dtype_code(v.dtype), float(eps), stream_of(v)),
+        "sy_bwd_batched",
+    )
+
+
+def merge_stats(o1, ms1, o2, ms2, o, ms, normalize: bool, rows: int, d: int) -> None:
+    check(
+        lib.sy_merge_stats(o1.data_ptr(), ms1.data_ptr(), o2.data_ptr(), ms2.data_ptr(),
+                           o.data_ptr(), ms.data_ptr() if ms is not None else None,
+                           1 if normalize else 0, rows, d, dtype_code(o1.dtype), stream_of(o1)),
+        "sy_merge_stats",
     )
 
 

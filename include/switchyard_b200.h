@@ -134,6 +134,56 @@ SY_API int sy_fwd_batched(const void* v, const void* queries, void* out, int64_t
                    sy_stream_t stream);
 
 /*
+ * Batched forward that also returns the merge statistics: as sy_fwd_batched,
+ * plus mstats[(s * BT + tok) * 2 + {0, 1}] = (m, l) = (max_n logit_{s,n},
+ * sum_n exp(logit_{s,n} - m)) in fp32 (8-byte aligned). raw = 0 writes the
+ * softmax average (the block_attn_res_batched output); raw = 1 writes the
+ * unnormalised o = sum_n exp(logit_{s,n} - m) v_n, so (out, m, l) is the
+ * (o, m, ell) triple of attn_with_stats (src/switchyard/reference.py:195-216)
+ * for each query. S >= 1 (S = 1 is attn_with_stats for one query). The
+ * reference's batched API returns no statistics (README.md:63-70); this is
+ * the first half of its "complete the batched training contract" item
+ * (PROJECT_STATE.md:74-75).
+ */
+SY_API int sy_fwd_batched_stats(const void* v, const void* queries, void* out,
+                                float* mstats, int raw, int64_t N, int64_t BT,
+                                int64_t D, int64_t S, int dtype, float eps,
+                                sy_stream_t stream);
+
+/* Number of fp32 dq partial rows (each S * D floats) sy_bwd_batched expects
+ * for a shape on the current device (>= 1), or -status. */
+SY_API int64_t sy_bwd_batched_partials(int64_t N, int64_t BT, int64_t D,
+                                       int64_t S, int dtype);
+
+/*
+ * Backward of the batched forward (sy_fwd_batched, or sy_fwd_batched_stats
+ * with raw = 0): the second half of the batched training contract the
+ * reference lacks (src/switchyard/triton_op.py:475-479 raises instead).
+ * g: gradient of out, [S, BT, D] in v's dtype. Writes dv [N, BT, D] in v's
+ * dtype and P = sy_bwd_batched_partials(..) fp32 partial rows dq_partial
+ * [P, S, D]; sy_dw_reduce(dq_partial, P, S * D, dq, dtype) then gives dq
+ * [S, D] in a fixed summation order. The dot products and the softmax are
+ * recomputed from v and the queries in one pass per token, so nothing is
+ * saved by the forward. S <= 16.
+ */
+SY_API int sy_bwd_batched(const void* v, const void* queries, const void* g,
+                          void* dv, float* dq_partial, int64_t P, int64_t N,
+                          int64_t BT, int64_t D, int64_t S, int dtype, float eps,
+                          sy_stream_t stream);
+
+/*
+ * Online-softmax merge of two partial results over disjoint source groups,
+ * R rows of D (merge_online_softmax, src/switchyard/reference.py:219-233):
+ * m = max(m1, m2), s_i = exp(m_i - m), o = o1 s1 + o2 s2, l = l1 s1 + l2 s2,
+ * with (m, l) pairs per row in ms1 / ms2 / ms (fp32, 8-byte aligned; ms may
+ * be NULL). normalize = 1 writes o / l (the finished output) instead of o.
+ * o must not alias o1 or o2.
+ */
+SY_API int sy_merge_stats(const void* o1, const float* ms1, const void* o2,
+                          const float* ms2, void* o, float* ms, int normalize,
+                          int64_t R, int64_t D, int dtype, sy_stream_t stream);
+
+/*
  * Speed-of-light ceiling: out[tok, d] = sum_n v[n, tok, d]. Same bytes and
  * access pattern as sy_fwd without the softmax. Replaces speed_of_light /
  * _speed_of_light (src/switchyard/triton_op.py:153-191).

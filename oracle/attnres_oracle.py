@@ -148,6 +148,28 @@ def batched(v, queries, eps: float = DEFAULT_EPS) -> np.ndarray:
     return np.einsum("snbt,nbtd->sbtd", alpha, v)
 
 
+def batched_stats(v, queries, eps: float = DEFAULT_EPS):
+    """Per-query ``(o, m, ell)`` triples, each with a leading ``S`` axis:
+    ``attn_with_stats`` (reference.py:195-216) applied to every query."""
+    res = [attn_with_stats(v, q, eps) for q in _f64(queries)]
+    return tuple(np.stack(x) for x in zip(*res))
+
+
+def batched_backward(v, queries, g, eps: float = DEFAULT_EPS):
+    """Gradients ``(dv, dqueries)`` of ``sum(batched(v, queries) * g)``, ``g``
+    of shape ``[S, B, T, D]``. Output ``s`` is ``forward(v, queries[s])``
+    (triton_op.py:460-461), so the loss is a sum of single-query losses and
+    ``dv = sum_s backward(v, q_s, g_s).dv``, ``dq_s = backward(v, q_s, g_s).dw``."""
+    v, q, g = _f64(v), _f64(queries), _f64(g)
+    dv = np.zeros_like(v)
+    dq = np.zeros_like(q)
+    for s in range(q.shape[0]):
+        dvs, dqs = backward(v, q[s], g[s], eps)
+        dv += dvs
+        dq[s] = dqs
+    return dv, dq
+
+
 def speed_of_light(v) -> np.ndarray:
     """``sum_n v_n``: the bytes of the forward without its softmax
     (triton_op.py:153-176)."""
