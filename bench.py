@@ -69,7 +69,8 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="CPU-baseline budget")
     ap.add_argument("--no-extras", action="store_true", help="skip batched/SoL/e2e extras")
-    ap.add_argument("--profile", choices=["fwd", "bwd", "step", "sol", "batched8", "batched16"],
+    ap.add_argument("--profile", choices=["fwd", "bwd", "step", "sol", "batched8", "batched16",
+                                          "batched_bwd8", "merge"],
                     default=None,
                     help="no timing: run 5 launches of one kernel (or step) at the representative "
                          "shape, for an ncu capture; prints nothing")
@@ -349,6 +350,112 @@ def batched_times(v, steps, flush, hbm_gbs, qs=(1, 4, 8, 16)):
     return out
 
 
+def batched_train_times(v, steps, flush, hbm_gbs, qs=(1, 4, 8, 16)):
+    """The batched training contract at Q queries: the backward alone
+    (sy_bwd_batched + the dq reduction, reads v and g, writes dv) and the whole
+    autograd step (block_attn_res_batched_train forward + backward), and the
+    two-phase schedule (attn_with_stats over the first N // 2 sources and the
+    rest, then merge_online_softmax with the division fused). Roofline as in
+    batched_times: the larger of the HBM time and the FP32 time, the backward
+    doing (5Q + 2) N multiply-adds per token element."""
+    from switchyard import _native, attn_with_stats, block_attn_res_batched_train
+    from switchyard import merge_online_softmax
+
+    n, b, t, d = v.shape
+    bt = b * t
+    props = torch.cuda.get_device_properties(v.device)
+    clock_mhz = load_peak_field("sm_max_mhz") or 1965.0
+    fp32_tflops = props.multi_processor_count * 128 * 2 * clock_mhz * 1e6 / 1e12
+    slab = bt * d * ITEM
+    out = {}
+    gen = torch.Generator(device=v.device).manual_seed(11)
+    for q in qs:
+        queries = (torch.randn(q, d, device=v.device, generator=gen) / math.sqrt(d)).to(v.dtype)
+        g = torch.randn(q, b, t, d, device=v.device, generator=gen).to(v.dtype)
+        p_rows = _native.bwd_batched_partials(n, bt, d, q, v.dtype)
+        part = torch.empty(p_rows, q * d, device=v.device, dtype=torch.float32)
+        dv = torch.empty_like(v)
+        dq = torch.empty_like(queries)
+
+        def bwd():
+            _native.bwd_batched(v, queries, g, dv, part, n, bt, d, q, 1e-6)
+            _native.dw_reduce(part, dq.view(q * d))
+
+        vt = v.detach().requires_grad_(True)
+        qt = queries.detach().requires_grad_(True)
+
+        def step():
+            vt.grad = None
+            qt.grad = None
+            block_attn_res_batched_train(vt, qt).backward(g)
+
+        res = {}
+        for name, fn, byts in (("bwd", bwd, (2 * n + q) * slab),
+                               ("step", step, (3 * n + 2 * q) * slab)):
+            for _ in range(3):
+                fn()
+            st = summarize(timed_steps(fn, steps, flush))
+            flops = 2 * (5 * q + 2) * n * bt * d + (2 + 4 * q) * n * bt * d * (name == "step")
+            t_hbm = byts / (hbm_gbs * 1e9) * 1e3
+            t_fp32 = flops / (fp32_tflops * 1e12) * 1e3
+            res[name] = {
+                "us": st["mean_ms"] * 1e3,
+                "tbps": byts / (st["mean_ms"] * 1e-3) / 1e12,
+                "bytes": byts,
+                "flops": flops,
+                "bound": "hbm" if t_hbm >= t_fp32 else "fp32",
+                "frac": max(t_hbm, t_fp32) / st["mean_ms"],
+            }
+        out[f"Q{q}"] = res
+    w = (torch.randn(d, device=v.device, generator=gen) / math.sqrt(d)).to(v.dtype)
+    k = n // 2
+
+    def two_phase():
+        o1, m1, l1 = attn_with_stats(v[:k], w)
+        o2, m2, l2 = attn_with_stats(v[k:], w)
+        return merge_online_softmax(o1, m1, l1, o2, m2, l2, normalize=True)
+
+    o1, m1, l1 = attn_with_stats(v[:k], w)
+    o2, m2, l2 = attn_with_stats(v[k:], w)
+    with torch.no_grad():
+        for name, fn, byts in (
+                ("two_phase", two_phase, (n + 5) * slab),
+                ("merge", lambda: merge_online_softmax(o1, m1, l1, o2, m2, l2, normalize=True),
+                 3 * slab)):
+            for _ in range(3):
+                fn()
+            st = summarize(timed_steps(fn, steps, flush))
+            out[name] = {"us": st["mean_ms"] * 1e3, "bytes": byts,
+                         "tbps": byts / (st["mean_ms"] * 1e-3) / 1e12,
+                         "frac": byts / (hbm_gbs * 1e9) / (st["mean_ms"] * 1e-3)}
+    return out
+
+
+def stage_times(v, steps, flush, hbm_gbs):
+    """The decoder's arena staging at one slab [B, T, D]: stage_partial (one
+    kernel: partial + out written to the new partial and the arena slot, 4 slab
+    passes) against the reference's partial + out then arena.copy_ (two
+    kernels, 5 slab passes)."""
+    from switchyard import stage_partial
+
+    n, b, t, d = v.shape
+    slab = b * t * d * ITEM
+    partial, out = v[0], v[1]
+    arena = torch.empty(2, b, t, d, device=v.device, dtype=v.dtype)
+    res = {}
+    with torch.no_grad():
+        for name, fn, byts in (
+                ("fused", lambda: stage_partial(partial, out, arena[1]), 4 * slab),
+                ("add_then_copy", lambda: arena[1].copy_(partial + out), 5 * slab)):
+            for _ in range(3):
+                fn()
+            st = summarize(timed_steps(fn, steps, flush))
+            res[name] = {"us": st["mean_ms"] * 1e3, "bytes": byts,
+                         "tbps": byts / (st["mean_ms"] * 1e-3) / 1e12,
+                         "frac": byts / (hbm_gbs * 1e9) / (st["mean_ms"] * 1e-3)}
+    return res
+
+
 def e2e_times(dev, steps, n, b, t, d, op):
     """Same step through the public API from pinned host buffers: H2D of v, w
     and dout, forward + backward, D2H of dw -- all inside the events."""
@@ -501,6 +608,8 @@ def run_ours(args):
         }
     if not args.no_extras and rank == 0:
         result["batched"] = batched_times(v, max(20, args.steps // 4), flush, peak)
+        result["batched_train"] = batched_train_times(v, max(10, args.steps // 10), flush, peak)
+        result["arena_stage"] = stage_times(v, max(20, args.steps // 4), flush, peak)
         e2e, h2d, d2h = e2e_times(dev, 10, n, b, t, d, block_attn_res_triton)
         result["e2e"] = {
             "value": tot_b / (e2e["mean_ms"] * 1e-3) / 1e12,
@@ -666,7 +775,8 @@ def run_profile(kind: str, shape: str | None = None):
     """A handful of launches at the representative shape (or `shape`,
     "N,B,T,D") and nothing else, so that an ncu capture ends by itself in
     seconds."""
-    from switchyard import _native, block_attn_res_batched, block_attn_res_triton
+    from switchyard import _native, attn_with_stats, block_attn_res_batched, block_attn_res_triton
+    from switchyard import merge_online_softmax
 
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -691,6 +801,17 @@ def run_profile(kind: str, shape: str | None = None):
             vv = v.detach().requires_grad_(True)
             ww = w.detach().requires_grad_(True)
             block_attn_res_triton(vv, ww).backward(dout)
+        elif kind == "batched_bwd8":
+            g8 = dout.unsqueeze(0).expand(8, b, t, d).contiguous() if _ == 0 else g8
+            p8 = _native.bwd_batched_partials(n, bt, d, 8, v.dtype)
+            part8 = torch.empty(p8, 8 * d, device=dev, dtype=torch.float32)
+            _native.bwd_batched(v, q[:8], g8, dv, part8, n, bt, d, 8, 1e-6)
+        elif kind == "merge":
+            with torch.no_grad():
+                if _ == 0:
+                    o1, m1, l1 = attn_with_stats(v[: n // 2], w)
+                    o2, m2, l2 = attn_with_stats(v[n // 2:], w)
+                merge_online_softmax(o1, m1, l1, o2, m2, l2, normalize=True)
         elif kind.startswith("batched"):
             with torch.no_grad():
                 block_attn_res_batched(v, q[: int(kind[len("batched"):])])

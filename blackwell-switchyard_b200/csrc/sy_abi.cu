@@ -767,7 +767,11 @@ int64_t sy_bwd_batched_partials(int64_t N, int64_t BT, int64_t D, int64_t S, int
   if (BT == 0 || D == 0) return 1;
   DevInfo di;
   if (dev_info(&di) != cudaSuccess) return -SY_ERR_CUDA;
-  const int64_t g = (int64_t)di.sms * 2;
+  // register tile: one CTA per SM (its dq columns live in shared memory);
+  // generic: two per SM
+  const int64_t g = reg_bwd_batched_fits((int)N, (int)D, (int)S, dtype, di.max_smem)
+                        ? (int64_t)di.sms
+                        : (int64_t)di.sms * 2;
   return BT < g ? BT : g;
 }
 
@@ -789,10 +793,36 @@ int sy_bwd_batched(const void* v, const void* queries, const void* g, void* dv,
   DevInfo di;
   cudaError_t e = dev_info(&di);
   if (e != cudaSuccess) return cuda_status(e, "sy_bwd_batched: device query");
+  if (reg_bwd_batched_fits((int)N, (int)D, (int)S, dtype, di.max_smem) && al16(v) && al16(queries) &&
+      al16(g) && al16(dv) && al16(dq_partial)) {
+    e = launch_reg_bwd_batched(BT, (int)N, (int)D, (int)S, dtype, v, queries, g, dv, dq_partial,
+                               (int)P, eps, st);
+    return cuda_status(e, "sy_bwd_batched: register-tile kernel launch");
+  }
   if (bwd_batched_smem((int)N, (int)S) > (size_t)di.max_smem) return SY_ERR_UNSUPPORTED;
   e = launch_bwd_batched(BT, (int)N, (int)D, (int)S, dtype, v, queries, g, dv, dq_partial, (int)P,
                          eps, st);
   return cuda_status(e, "sy_bwd_batched: kernel launch");
+}
+
+int sy_stage_partial(const void* partial, const void* out, void* new_partial, void* arena_slot,
+                     int64_t numel, int dtype, sy_stream_t stream) {
+  if (!esize_of(dtype)) return SY_ERR_DTYPE;
+  if (numel < 0) return SY_ERR_ARG;
+  if (numel == 0) return SY_OK;
+  if (!partial || !out || !arena_slot) return SY_ERR_ARG;
+  DevInfo di;
+  cudaError_t e = dev_info(&di);
+  if (e != cudaSuccess) return cuda_status(e, "sy_stage_partial: device query");
+  const int es = esize_of(dtype);
+  const bool vec16 = (numel * es) % 16 == 0 && al16(partial) && al16(out) && al16(arena_slot) &&
+                     (new_partial == nullptr || al16(new_partial));
+  const int64_t work = vec16 ? numel * es / 16 : numel;
+  const int64_t cap = (int64_t)di.sms * 8;  // 8 CTAs of 256 threads per SM
+  const int64_t blocks = (work + 255) / 256;
+  e = launch_stage(numel, dtype, partial, out, new_partial, arena_slot, vec16,
+                   (int)(blocks < cap ? blocks : cap), static_cast<cudaStream_t>(stream));
+  return cuda_status(e, "sy_stage_partial: kernel launch");
 }
 
 int sy_merge_stats(const void* o1, const float* ms1, const void* o2, const float* ms2, void* o,
@@ -807,8 +837,10 @@ int sy_merge_stats(const void* o1, const float* ms1, const void* o2, const float
   DevInfo di;
   cudaError_t e = dev_info(&di);
   if (e != cudaSuccess) return cuda_status(e, "sy_merge_stats: device query");
-  e = launch_merge(R, (int)D, dtype, o1, ms1, o2, ms2, o, ms, normalize, generic_grid(R, di),
-                   static_cast<cudaStream_t>(stream));
+  const int vec16 = (D * esize_of(dtype)) % 16 == 0 && al16(o1) && al16(o2) && al16(o);
+  const int64_t cap = (int64_t)di.sms * 8;  // one row per CTA, 8 CTAs per SM in flight
+  e = launch_merge(R, (int)D, dtype, o1, ms1, o2, ms2, o, ms, normalize, vec16,
+                   (int)(R < cap ? R : cap), static_cast<cudaStream_t>(stream));
   return cuda_status(e, "sy_merge_stats: kernel launch");
 }
 

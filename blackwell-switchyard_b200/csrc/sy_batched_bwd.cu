@@ -25,6 +25,7 @@
 // src/switchyard/reference.py:219-233) on (o, m, l) triples, one CTA per row,
 // with the final o / l division optionally fused.
 #include "sy_launch.cuh"
+#include "sy_reg.cuh"
 #include "sy_tile.cuh"
 
 namespace sy {
@@ -169,6 +170,246 @@ __global__ void __launch_bounds__(kGenericThreads)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Register-tile variant for rows of at most 256 16-byte chunks (4 KiB) and
+// N <= kBwdRegMaxN: thread t owns chunk t of every row of the token, so the
+// token's N source chunks are read from HBM once, into registers, and every
+// dot product, dv and the thread's columns of dq come from them.
+//
+//   * sums of squares: one 16-value reduce-scatter per warp;
+//   * per query s: q_s . v_n and g_s . v_n (packed 16-bit FMA into fp32) for
+//     all n, one 32-value reduce-scatter (values 0..15: q dots, 16..31: g dots);
+//     warp totals to shared memory, summed over the 8 warps in warp order;
+//   * coefficients: warp w takes queries w, w + 8, ...; lane n source n;
+//   * dv_n = sum_s (alpha_{s,n} g_s + da_{s,n} q_s) + cv_n v_n in fp32
+//     registers, one rounding; dq_s's columns of this thread accumulate in
+//     shared memory (thread-private, no barrier) over the CTA's tokens and are
+//     written once as the CTA's partial row.
+// ---------------------------------------------------------------------------
+constexpr int kBwdRegMaxN = 9;  // no spills for any dtype up to here (fp16 spills from 10)
+
+template <typename T>
+__device__ __forceinline__ float dot_chunk(const uint4& a, const uint4& b) {
+  if constexpr (sizeof(T) == 2) {
+    float2 acc = make_float2(0.f, 0.f);
+    mixfma2<T>(acc, a.x, b.x);
+    mixfma2<T>(acc, a.y, b.y);
+    mixfma2<T>(acc, a.z, b.z);
+    mixfma2<T>(acc, a.w, b.w);
+    return acc.x + acc.y;
+  } else {
+    const float4 x = *reinterpret_cast<const float4*>(&a);
+    const float4 y = *reinterpret_cast<const float4*>(&b);
+    float2 acc = make_float2(x.x * y.x, x.y * y.y);
+    acc = __ffma2_rn(make_float2(x.z, x.w), make_float2(y.z, y.w), acc);
+    return acc.x + acc.y;
+  }
+}
+
+struct RegBwdSmem {
+  size_t q_off, dq_off, red_off, coef_off, cvp_off, total;
+};
+__host__ __device__ inline RegBwdSmem reg_bwd_batched_layout(int N, int S, int rc, int vec) {
+  RegBwdSmem L;
+  L.q_off = 0;                                                   // [S][rc] uint4
+  L.dq_off = L.q_off + (size_t)S * rc * 16;                      // [S][rc * vec] fp32
+  L.red_off = L.dq_off + (size_t)S * rc * vec * 4;               // [S + 1][8][32] fp32
+  L.coef_off = L.red_off + (size_t)(S + 1) * kBW * 32 * 4;      // [S][N] float2
+  L.cvp_off = L.coef_off + (size_t)S * N * 8;                    // [S][N] fp32
+  L.total = L.cvp_off + (size_t)S * N * 4;
+  return L;
+}
+
+template <typename T, int N>
+__global__ void __launch_bounds__(kGenericThreads, 1)
+    reg_bat_bwd_kernel(const T* __restrict__ v, const T* __restrict__ q, const T* __restrict__ g,
+                       T* __restrict__ dv, float* __restrict__ dq_partial, long long BT, int D,
+                       int S, int rc, float eps) {
+  constexpr int VEC = Dt<T>::kVec;
+  constexpr int P = VEC / 2;
+  extern __shared__ __align__(16) unsigned char rsm[];
+  const RegBwdSmem L = reg_bwd_batched_layout(N, S, rc, VEC);
+  uint4* qs = reinterpret_cast<uint4*>(rsm + L.q_off);
+  float* dqs = reinterpret_cast<float*>(rsm + L.dq_off);
+  float* red = reinterpret_cast<float*>(rsm + L.red_off);
+  float2* coef = reinterpret_cast<float2*>(rsm + L.coef_off);
+  float* cvp = reinterpret_cast<float*>(rsm + L.cvp_off);
+  const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+  const bool act = tid < rc;
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  for (int i = tid; i < S * rc; i += kGenericThreads)
+    qs[i] = reinterpret_cast<const uint4*>(q)[i];
+  for (int i = tid; i < S * rc * VEC; i += kGenericThreads) dqs[i] = 0.f;
+  __syncthreads();
+  const float inv_d = 1.f / (float)D;
+  for (long long tok = blockIdx.x; tok < BT; tok += gridDim.x) {
+    uint4 vx[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n)
+      vx[n] = act ? reinterpret_cast<const uint4*>(v + ((size_t)n * BT + tok) * D)[tid] : z4;
+    {
+      float sv[16];
+#pragma unroll
+      for (int n = 0; n < 16; ++n) sv[n] = n < N ? dot_chunk<T>(vx[n], vx[n]) : 0.f;
+      const float t = warp_reduce_scatter16(sv, lane);
+      if ((lane & 1) == 0 && (lane >> 1) < N) red[((size_t)S * kBW + wp) * 32 + (lane >> 1)] = t;
+    }
+    // g_{s+1}'s chunk is requested before g_s's dots are reduced (one query
+    // ahead), so its latency overlaps the reduction instead of following it
+    const uint4* gcol = reinterpret_cast<const uint4*>(g + (size_t)tok * D) + tid;
+    const size_t gstride = (size_t)BT * D / Dt<T>::kVec;  // one query's slab, in chunks
+    uint4 gnext = act ? gcol[0] : z4;
+    for (int s = 0; s < S; ++s) {
+      const uint4 gx = gnext;
+      if (act && s + 1 < S) gnext = gcol[(size_t)(s + 1) * gstride];
+      const uint4 qx = act ? qs[s * rc + tid] : z4;
+      float a[32];
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        a[n] = n < N ? dot_chunk<T>(qx, vx[n]) : 0.f;
+        a[16 + n] = n < N ? dot_chunk<T>(gx, vx[n]) : 0.f;
+      }
+      const float t = warp_reduce_scatter<32>(a, lane);
+      if ((lane & 15) < N) red[((size_t)s * kBW + wp) * 32 + lane] = t;
+    }
+    __syncthreads();
+    for (int s = wp; s < S; s += kBW) {
+      const bool on = lane < N;
+      const int n = on ? lane : 0;
+      float a = 0.f, G = 0.f, ssq = 0.f;
+      for (int k = 0; k < kBW; ++k) {
+        a += red[((size_t)s * kBW + k) * 32 + n];
+        G += red[((size_t)s * kBW + k) * 32 + 16 + n];
+        ssq += red[((size_t)S * kBW + k) * 32 + n];
+      }
+      const float r = rsqrtf(ssq * inv_d + eps);
+      const float lg = a * r;
+      const float m = warp_max(on ? lg : -INFINITY);
+      const float e = on ? expf(lg - m) : 0.f;
+      const float al = e / warp_sum(e);
+      const float delta = warp_sum(on ? al * G : 0.f);
+      const float dl = al * (G - delta);
+      if (on) {
+        coef[s * N + n] = make_float2(al, dl * r);
+        cvp[s * N + n] = -dl * lg * r * r * inv_d;
+      }
+    }
+    __syncthreads();
+    float2 acc[N][P];
+    float cvn[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+      cvn[n] = 0.f;
+#pragma unroll
+      for (int i = 0; i < P; ++i) acc[n][i] = make_float2(0.f, 0.f);
+    }
+    gnext = act ? gcol[0] : z4;
+    for (int s = 0; s < S; ++s) {
+      const uint4 gx = gnext;
+      if (act && s + 1 < S) gnext = gcol[(size_t)(s + 1) * gstride];
+      const uint4 qx = act ? qs[s * rc + tid] : z4;
+      float2 gf[P], qf[P], dqp[P];
+      unpack2<T>(gx, gf);
+      unpack2<T>(qx, qf);
+#pragma unroll
+      for (int i = 0; i < P; ++i) dqp[i] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int n = 0; n < N; ++n) {
+        const float2 cf = coef[s * N + n];
+        cvn[n] += cvp[s * N + n];
+        float2 vf[P];
+        unpack2<T>(vx[n], vf);
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+          acc[n][i] = __ffma2_rn(f2(cf.x), gf[i], acc[n][i]);
+          acc[n][i] = __ffma2_rn(f2(cf.y), qf[i], acc[n][i]);
+          dqp[i] = __ffma2_rn(f2(cf.y), vf[i], dqp[i]);
+        }
+      }
+      if (act) {
+        float2* dq2 = reinterpret_cast<float2*>(dqs + (size_t)s * rc * VEC + (size_t)tid * VEC);
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+          const float2 o = dq2[i];
+          dq2[i] = make_float2(o.x + dqp[i].x, o.y + dqp[i].y);
+        }
+      }
+    }
+    if (act) {
+#pragma unroll
+      for (int n = 0; n < N; ++n) {
+        float2 vf[P];
+        unpack2<T>(vx[n], vf);
+#pragma unroll
+        for (int i = 0; i < P; ++i) acc[n][i] = __ffma2_rn(f2(cvn[n]), vf[i], acc[n][i]);
+        reinterpret_cast<uint4*>(dv + ((size_t)n * BT + tok) * D)[tid] = pack2<T>(acc[n]);
+      }
+    }
+  }
+  if (act) {
+    float* prow = dq_partial + (size_t)blockIdx.x * S * D;
+    for (int s = 0; s < S; ++s) {
+      const float4* src = reinterpret_cast<const float4*>(dqs + (size_t)s * rc * VEC + (size_t)tid * VEC);
+      float4* dst = reinterpret_cast<float4*>(prow + (size_t)s * D + (size_t)tid * VEC);
+#pragma unroll
+      for (int i = 0; i < VEC / 4; ++i) dst[i] = src[i];
+    }
+  }
+}
+
+template <typename T, int N>
+static cudaError_t launch_reg_bat_bwd_n(long long BT, int D, int S, int rc, const void* v,
+                                        const void* q, const void* g, void* dv, float* dqp, int P,
+                                        float eps, cudaStream_t st) {
+  const size_t smem = reg_bwd_batched_layout(N, S, rc, Dt<T>::kVec).total;
+  return launch_smem(reg_bat_bwd_kernel<T, N>, P, kGenericThreads, smem, st,
+                     static_cast<const T*>(v), static_cast<const T*>(q), static_cast<const T*>(g),
+                     static_cast<T*>(dv), dqp, BT, D, S, rc, eps);
+}
+
+template <typename T>
+static cudaError_t launch_reg_bat_bwd_t(int N, long long BT, int D, int S, int rc, const void* v,
+                                        const void* q, const void* g, void* dv, float* dqp, int P,
+                                        float eps, cudaStream_t st) {
+  switch (N) {
+#define SY_RB_CASE(k) \
+  case k:             \
+    return launch_reg_bat_bwd_n<T, k>(BT, D, S, rc, v, q, g, dv, dqp, P, eps, st);
+    SY_RB_CASE(1) SY_RB_CASE(2) SY_RB_CASE(3) SY_RB_CASE(4) SY_RB_CASE(5) SY_RB_CASE(6)
+    SY_RB_CASE(7) SY_RB_CASE(8) SY_RB_CASE(9)
+#undef SY_RB_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+// Whether the register-tile variant takes a shape: rows of whole 16-byte
+// chunks, at most one chunk per thread, N <= kBwdRegMaxN, S <= 16, and its
+// shared memory within the device's opt-in limit.
+bool reg_bwd_batched_fits(int N, int D, int S, int dtype, int max_smem) {
+  const int es = dtype == SY_F32 ? 4 : 2;
+  if (N < 1 || N > kBwdRegMaxN || S < 1 || S > kBwdBatchedMaxS || (D * es) % 16) return false;
+  const int rc = D * es / 16;
+  if (rc > kGenericThreads) return false;
+  return reg_bwd_batched_layout(N, S, rc, 16 / es).total <= (size_t)max_smem;
+}
+
+cudaError_t launch_reg_bwd_batched(long long BT, int N, int D, int S, int dtype, const void* v,
+                                   const void* q, const void* g, void* dv, float* dq_partial,
+                                   int P, float eps, cudaStream_t st) {
+  const int rc = D * (dtype == SY_F32 ? 4 : 2) / 16;
+  switch (dtype) {
+    case SY_BF16:
+      return launch_reg_bat_bwd_t<__nv_bfloat16>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps, st);
+    case SY_F16:
+      return launch_reg_bat_bwd_t<__half>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps, st);
+    case SY_F32:
+      return launch_reg_bat_bwd_t<float>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps, st);
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
 size_t bwd_batched_smem(int N, int S) {
   return ((size_t)N * (2 * S + 1) * kBW + 3 * (size_t)S * N + 2 * (size_t)N) * sizeof(float);
 }
@@ -180,8 +421,19 @@ template <typename T>
 __global__ void __launch_bounds__(kGenericThreads)
     merge_kernel(const T* __restrict__ o1, const float* __restrict__ ms1, const T* __restrict__ o2,
                  const float* __restrict__ ms2, T* __restrict__ o, float* __restrict__ ms,
-                 long long R, int D, int normalize) {
+                 long long R, int D, int normalize, int vec16) {
+  constexpr int P = Dt<T>::kVec / 2;
+  const int rc = vec16 ? D / Dt<T>::kVec : 0;
   for (long long row = blockIdx.x; row < R; row += gridDim.x) {
+    const size_t base = (size_t)row * D;
+    // the rows' first chunks are requested before the statistics are used,
+    // so the two loads overlap instead of running back to back
+    const int k0 = threadIdx.x;
+    uint4 xa = make_uint4(0u, 0u, 0u, 0u), xb = xa;
+    if (k0 < rc) {
+      xa = reinterpret_cast<const uint4*>(o1 + base)[k0];
+      xb = reinterpret_cast<const uint4*>(o2 + base)[k0];
+    }
     const float2 a = reinterpret_cast<const float2*>(ms1)[row];
     const float2 b = reinterpret_cast<const float2*>(ms2)[row];
     const float m = fmaxf(a.x, b.x);
@@ -193,10 +445,25 @@ __global__ void __launch_bounds__(kGenericThreads)
       c1 *= inv;
       c2 *= inv;
     }
-    const size_t base = (size_t)row * D;
-    for (int d = threadIdx.x; d < D; d += kGenericThreads)
-      o[base + d] = Dt<T>::from_f(
-          fmaf(Dt<T>::to_f(o1[base + d]), c1, Dt<T>::to_f(o2[base + d]) * c2));
+    if (vec16) {  // rows of whole 16-byte chunks, 16-byte aligned
+      uint4* c4 = reinterpret_cast<uint4*>(o + base);
+      for (int k = k0; k < rc; k += kGenericThreads) {
+        if (k != k0) {
+          xa = reinterpret_cast<const uint4*>(o1 + base)[k];
+          xb = reinterpret_cast<const uint4*>(o2 + base)[k];
+        }
+        float2 x[P], y[P];
+        unpack2<T>(xa, x);
+        unpack2<T>(xb, y);
+#pragma unroll
+        for (int i = 0; i < P; ++i) x[i] = __ffma2_rn(x[i], f2(c1), __fmul2_rn(y[i], f2(c2)));
+        c4[k] = pack2<T>(x);
+      }
+    } else {
+      for (int d = threadIdx.x; d < D; d += kGenericThreads)
+        o[base + d] = Dt<T>::from_f(
+            fmaf(Dt<T>::to_f(o1[base + d]), c1, Dt<T>::to_f(o2[base + d]) * c2));
+    }
     if (ms != nullptr && threadIdx.x == 0)
       reinterpret_cast<float2*>(ms)[row] = make_float2(m, l);
   }
@@ -234,12 +501,12 @@ cudaError_t launch_bwd_batched(long long BT, int N, int D, int S, int dtype, con
 
 cudaError_t launch_merge(long long R, int D, int dtype, const void* o1, const float* ms1,
                          const void* o2, const float* ms2, void* o, float* ms, int normalize,
-                         int grid, cudaStream_t st) {
+                         int vec16, int grid, cudaStream_t st) {
   SY_BB_DTYPE_SWITCH(dtype, T,
                      return launch_smem(merge_kernel<T>, grid, kGenericThreads, 0, st,
                                         static_cast<const T*>(o1), ms1,
                                         static_cast<const T*>(o2), ms2, static_cast<T*>(o), ms, R,
-                                        D, normalize))
+                                        D, normalize, vec16))
 }
 
 }  // namespace sy

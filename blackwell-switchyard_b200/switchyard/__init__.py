@@ -14,6 +14,7 @@ from .triton_op import (
     block_attn_res_triton,
     speed_of_light,
 )
+from .arena import stage_partial
 from .two_phase import attn_with_stats, block_attn_res_batched_train, merge_online_softmax
 
 __version__ = "0.1.0"
@@ -28,4 +29,5 @@ __all__ = [
     "attn_with_stats",
     "merge_online_softmax",
     "block_attn_res_batched_train",
+    "stage_partial",
 ]

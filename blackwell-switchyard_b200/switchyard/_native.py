@@ -42,6 +42,7 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sy_bwd_batched_partials": ([_I64, _I64, _I64, _I64, _I], _I64),
     "sy_bwd_batched": ([_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I64, _I, _F, _P], _I),
     "sy_merge_stats": ([_P, _P, _P, _P, _P, _P, _I, _I64, _I64, _I, _P], _I),
+    "sy_stage_partial": ([_P, _P, _P, _P, _I64, _I, _P], _I),
     "sy_speed_of_light": ([_P, _P, _I64, _I64, _I64, _I, _P], _I),
     "sy_plan_kind": ([_I, _I64, _I64, _I64, _I64, _I], _I),
     "sy_plan_info": ([_I, _I64, _I64, _I64, _I64, _I, _I, _I, _c.POINTER(_I64)], _I),
@@ -199,6 +200,16 @@ def merge_stats(o1, ms1, o2, ms2, o, ms, normalize: bool, rows: int, d: int) -> 
                            o.data_ptr(), ms.data_ptr() if ms is not None else None,
                            1 if normalize else 0, rows, d, dtype_code(o1.dtype), stream_of(o1)),
         "sy_merge_stats",
+    )
+
+
+def stage_partial(partial, out, new_partial, arena_slot) -> None:
+    check(
+        lib.sy_stage_partial(partial.data_ptr(), out.data_ptr(),
+                             new_partial.data_ptr() if new_partial is not None else None,
+                             arena_slot.data_ptr(), partial.numel(), dtype_code(partial.dtype),
+                             stream_of(partial)),
+        "sy_stage_partial",
     )
 
 

@@ -35,6 +35,7 @@ import torch
 
 from . import _native
 from .triton_op import DEFAULT_EPS
+from .triton_op import _BlockAttnResTriton as _BlockAttnResTritonFn
 
 __all__ = ["attn_with_stats", "merge_online_softmax", "block_attn_res_batched_train"]
 
@@ -102,6 +103,26 @@ def attn_with_stats(v: torch.Tensor, w: torch.Tensor, eps: float = DEFAULT_EPS):
     return o, m, ell
 
 
+def _contiguous_strides(shape) -> tuple:
+    strides, acc = [], 1
+    for n in reversed(shape):
+        strides.append(acc)
+        acc *= n
+    return tuple(reversed(strides))
+
+
+def _pairs(m: torch.Tensor, ell: torch.Tensor, rows: int) -> torch.Tensor:
+    """The statistics as one fp32 ``[rows, 2]`` tensor of (m, ell) pairs. The
+    views :func:`attn_with_stats` returns already are that buffer (ell one
+    float after m, both with every stride doubled): it is used in place, with
+    no copy kernel; any other pair of tensors is stacked."""
+    if (m.dtype == ell.dtype == torch.float32 and m.device == ell.device
+            and ell.data_ptr() == m.data_ptr() + 4 and m.stride() == ell.stride()
+            and m.stride() == tuple(2 * x for x in _contiguous_strides(m.shape))):
+        return m.as_strided((rows, 2), (2, 1))
+    return torch.stack((m.float(), ell.float()), -1).reshape(rows, 2)
+
+
 def merge_online_softmax(o1, m1, l1, o2, m2, l2, normalize: bool = False):
     """Combine two ``(o, m, ell)`` triples over disjoint source groups, exactly.
 
@@ -125,8 +146,8 @@ def merge_online_softmax(o1, m1, l1, o2, m2, l2, normalize: bool = False):
     _native.dtype_code(o1.dtype)
     d = o1.shape[-1]
     rows = math.prod(lead)
-    ms1 = torch.stack((m1.float(), l1.float()), -1).reshape(rows, 2)
-    ms2 = torch.stack((m2.float(), l2.float()), -1).reshape(rows, 2)
+    ms1 = _pairs(m1, l1, rows)
+    ms2 = _pairs(m2, l2, rows)
     o1c = o1.contiguous()
     o2c = o2.contiguous()
     o = torch.empty_like(o1c)
@@ -181,4 +202,10 @@ def block_attn_res_batched_train(
     entry ``s`` equal to ``block_attn_res_triton(v, queries[s], eps)``, and
     gradients for ``v`` and ``queries`` (``S <= 16``). Same validation and
     messages as the reference's batched API (``triton_op.py:463-474``)."""
+    if queries.ndim == 2 and queries.shape[0] == 1:
+        # one query: the single-query operator's kernels (the same forward
+        # kernel block_attn_res_batched runs for S = 1, and its backward from
+        # saved statistics), queries' gradient through the index
+        _check_batched(v, queries)
+        return _BlockAttnResTritonFn.apply(v, queries[0], eps).unsqueeze(0)
     return _BlockAttnResBatched.apply(v, queries, eps)

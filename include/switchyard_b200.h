@@ -184,6 +184,18 @@ SY_API int sy_merge_stats(const void* o1, const float* ms1, const void* o2,
                           int64_t R, int64_t D, int dtype, sy_stream_t stream);
 
 /*
+ * The decoder's arena staging step in one pass: new_partial = partial + out
+ * (fp32 add, one rounding to dtype) written to new_partial and to arena_slot,
+ * numel elements each. Replaces `partial = partial + out` followed by
+ * `arena[len(blocks)].copy_(partial)` (src/switchyard/model.py:532-535):
+ * 4 slab passes in one launch instead of 5 in two. new_partial may be NULL
+ * (only the arena slot is written). No buffer may overlap another.
+ */
+SY_API int sy_stage_partial(const void* partial, const void* out, void* new_partial,
+                            void* arena_slot, int64_t numel, int dtype,
+                            sy_stream_t stream);
+
+/*
  * Speed-of-light ceiling: out[tok, d] = sum_n v[n, tok, d]. Same bytes and
  * access pattern as sy_fwd without the softmax. Replaces speed_of_light /
  * _speed_of_light (src/switchyard/triton_op.py:153-191).

@@ -53,3 +53,11 @@ def test_public_names_match_the_reference_module():
     for name in ("block_attn_res_triton", "block_attn_res_batched", "BlockAttnResTriton",
                  "speed_of_light", "_BlockAttnResTriton"):
         assert hasattr(op, name)
+
+
+def test_stage_partial_rejects_cpu_tensors():
+    from switchyard import stage_partial
+
+    a = torch.zeros(4, 8)
+    with pytest.raises(ValueError, match="CUDA"):
+        stage_partial(a, a, torch.zeros(4, 8))

@@ -37,8 +37,12 @@ NAMES = {torch.bfloat16: "bfloat16", torch.float16: "float16", torch.float32: "f
 # Shapes that reach each batched kernel: the register tile (N <= 16, rows of
 # 16-byte chunks that fit it), the row stream (N = 17, 8 KiB rows), the generic
 # kernel (D = 777: rows not a multiple of 16 bytes) and small odd shapes.
+# The backward: its register-tile kernel (N <= 9, rows of at most 4 KiB in
+# whole 16-byte chunks, including rows of fewer chunks than threads: D = 1000)
+# and its generic kernel (N = 17, D = 777, fp32 rows of 8 KiB).
 CASES = [((9, 1, 16, 2048), 8), ((9, 1, 24, 2048), 16), ((17, 1, 8, 4096), 8),
-         ((5, 1, 17, 777), 3), ((3, 2, 5, 64), 5), ((9, 1, 32, 2048), 1), ((4, 1, 9, 512), 2)]
+         ((5, 1, 17, 777), 3), ((3, 2, 5, 64), 5), ((9, 1, 32, 2048), 1), ((4, 1, 9, 512), 2),
+         ((6, 1, 40, 1000), 4)]
 
 
 def np64(t: torch.Tensor) -> np.ndarray:
