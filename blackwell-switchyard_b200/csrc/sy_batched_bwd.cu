@@ -186,7 +186,8 @@ __global__ void __launch_bounds__(kGenericThreads)
 //     shared memory (thread-private, no barrier) over the CTA's tokens and are
 //     written once as the CTA's partial row.
 // ---------------------------------------------------------------------------
-constexpr int kBwdRegMaxN = 9;  // no spills for any dtype up to here (fp16 spills from 10)
+constexpr int kBwdRegMaxN = 9;
+int reg_bwd_batched_ctas_per_sm(int N, int D, int S, int dtype, int max_smem);  // no spills for any dtype up to here (fp16 spills from 10)
 
 template <typename T>
 __device__ __forceinline__ float dot_chunk(const uint4& a, const uint4& b) {
@@ -220,8 +221,8 @@ __host__ __device__ inline RegBwdSmem reg_bwd_batched_layout(int N, int S, int r
   return L;
 }
 
-template <typename T, int N>
-__global__ void __launch_bounds__(kGenericThreads, 1)
+template <typename T, int N, int MINB>
+__global__ void __launch_bounds__(kGenericThreads, MINB)
     reg_bat_bwd_kernel(const T* __restrict__ v, const T* __restrict__ q, const T* __restrict__ g,
                        T* __restrict__ dv, float* __restrict__ dq_partial, long long BT, int D,
                        int S, int rc, float eps) {
@@ -295,54 +296,72 @@ __global__ void __launch_bounds__(kGenericThreads, 1)
       }
     }
     __syncthreads();
-    float2 acc[N][P];
+    // MINB = 2: dv in two halves of the chunk (H float2 pairs each), so only
+    // N * H fp32 pairs of accumulators are live and two CTAs fit an SM's
+    // registers; g_s is re-read per half (from L2), q_s from shared memory.
+    // MINB = 1 (shared memory holds one CTA anyway): the whole chunk at once.
+    constexpr int H = (MINB == 2 && P / 2 > 0) ? P / 2 : P;
     float cvn[N];
 #pragma unroll
-    for (int n = 0; n < N; ++n) {
-      cvn[n] = 0.f;
+    for (int n = 0; n < N; ++n) cvn[n] = 0.f;
 #pragma unroll
-      for (int i = 0; i < P; ++i) acc[n][i] = make_float2(0.f, 0.f);
-    }
-    gnext = act ? gcol[0] : z4;
-    for (int s = 0; s < S; ++s) {
-      const uint4 gx = gnext;
-      if (act && s + 1 < S) gnext = gcol[(size_t)(s + 1) * gstride];
-      const uint4 qx = act ? qs[s * rc + tid] : z4;
-      float2 gf[P], qf[P], dqp[P];
-      unpack2<T>(gx, gf);
-      unpack2<T>(qx, qf);
+    for (int h = 0; h < P / H; ++h) {
+      float2 acc[N][H];
 #pragma unroll
-      for (int i = 0; i < P; ++i) dqp[i] = make_float2(0.f, 0.f);
+      for (int n = 0; n < N; ++n)
 #pragma unroll
-      for (int n = 0; n < N; ++n) {
-        const float2 cf = coef[s * N + n];
-        cvn[n] += cvp[s * N + n];
-        float2 vf[P];
-        unpack2<T>(vx[n], vf);
+        for (int i = 0; i < H; ++i) acc[n][i] = make_float2(0.f, 0.f);
+      gnext = act ? gcol[0] : z4;
+      for (int s = 0; s < S; ++s) {
+        const uint4 gx = gnext;
+        if (act && s + 1 < S) gnext = gcol[(size_t)(s + 1) * gstride];
+        const uint4 qx = act ? qs[s * rc + tid] : z4;
+        float2 gf[P], qf[P], dqp[H];
+        unpack2<T>(gx, gf);
+        unpack2<T>(qx, qf);
 #pragma unroll
-        for (int i = 0; i < P; ++i) {
-          acc[n][i] = __ffma2_rn(f2(cf.x), gf[i], acc[n][i]);
-          acc[n][i] = __ffma2_rn(f2(cf.y), qf[i], acc[n][i]);
-          dqp[i] = __ffma2_rn(f2(cf.y), vf[i], dqp[i]);
+        for (int i = 0; i < H; ++i) dqp[i] = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int n = 0; n < N; ++n) {
+          const float2 cf = coef[s * N + n];
+          if (h == 0) cvn[n] += cvp[s * N + n];
+          float2 vf[P];
+          unpack2<T>(vx[n], vf);
+#pragma unroll
+          for (int i = 0; i < H; ++i) {
+            acc[n][i] = __ffma2_rn(f2(cf.x), gf[h * H + i], acc[n][i]);
+            acc[n][i] = __ffma2_rn(f2(cf.y), qf[h * H + i], acc[n][i]);
+            dqp[i] = __ffma2_rn(f2(cf.y), vf[h * H + i], dqp[i]);
+          }
+        }
+        if (act) {
+          float2* dq2 =
+              reinterpret_cast<float2*>(dqs + (size_t)s * rc * VEC + (size_t)tid * VEC) + h * H;
+#pragma unroll
+          for (int i = 0; i < H; ++i) {
+            const float2 o = dq2[i];
+            dq2[i] = make_float2(o.x + dqp[i].x, o.y + dqp[i].y);
+          }
         }
       }
       if (act) {
-        float2* dq2 = reinterpret_cast<float2*>(dqs + (size_t)s * rc * VEC + (size_t)tid * VEC);
 #pragma unroll
-        for (int i = 0; i < P; ++i) {
-          const float2 o = dq2[i];
-          dq2[i] = make_float2(o.x + dqp[i].x, o.y + dqp[i].y);
+        for (int n = 0; n < N; ++n) {
+          float2 vf[P];
+          unpack2<T>(vx[n], vf);
+          float2 o[P];
+#pragma unroll
+          for (int i = 0; i < P; ++i) o[i] = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int i = 0; i < H; ++i) o[h * H + i] = __ffma2_rn(f2(cvn[n]), vf[h * H + i], acc[n][i]);
+          const uint4 pk = pack2<T>(o);
+          if constexpr (H == P) {  // the whole 16-byte chunk
+            reinterpret_cast<uint4*>(dv + ((size_t)n * BT + tok) * D)[tid] = pk;
+          } else {  // this half's 8 bytes of the 16-byte chunk
+            uint2* dst = reinterpret_cast<uint2*>(dv + ((size_t)n * BT + tok) * D) + 2 * tid + h;
+            *dst = h == 0 ? make_uint2(pk.x, pk.y) : make_uint2(pk.z, pk.w);
+          }
         }
-      }
-    }
-    if (act) {
-#pragma unroll
-      for (int n = 0; n < N; ++n) {
-        float2 vf[P];
-        unpack2<T>(vx[n], vf);
-#pragma unroll
-        for (int i = 0; i < P; ++i) acc[n][i] = __ffma2_rn(f2(cvn[n]), vf[i], acc[n][i]);
-        reinterpret_cast<uint4*>(dv + ((size_t)n * BT + tok) * D)[tid] = pack2<T>(acc[n]);
       }
     }
   }
@@ -360,9 +379,13 @@ __global__ void __launch_bounds__(kGenericThreads, 1)
 template <typename T, int N>
 static cudaError_t launch_reg_bat_bwd_n(long long BT, int D, int S, int rc, const void* v,
                                         const void* q, const void* g, void* dv, float* dqp, int P,
-                                        float eps, cudaStream_t st) {
+                                        float eps, int ctas, cudaStream_t st) {
   const size_t smem = reg_bwd_batched_layout(N, S, rc, Dt<T>::kVec).total;
-  return launch_smem(reg_bat_bwd_kernel<T, N>, P, kGenericThreads, smem, st,
+  if (ctas == 2)
+    return launch_smem(reg_bat_bwd_kernel<T, N, 2>, P, kGenericThreads, smem, st,
+                       static_cast<const T*>(v), static_cast<const T*>(q), static_cast<const T*>(g),
+                       static_cast<T*>(dv), dqp, BT, D, S, rc, eps);
+  return launch_smem(reg_bat_bwd_kernel<T, N, 1>, P, kGenericThreads, smem, st,
                      static_cast<const T*>(v), static_cast<const T*>(q), static_cast<const T*>(g),
                      static_cast<T*>(dv), dqp, BT, D, S, rc, eps);
 }
@@ -370,11 +393,11 @@ static cudaError_t launch_reg_bat_bwd_n(long long BT, int D, int S, int rc, cons
 template <typename T>
 static cudaError_t launch_reg_bat_bwd_t(int N, long long BT, int D, int S, int rc, const void* v,
                                         const void* q, const void* g, void* dv, float* dqp, int P,
-                                        float eps, cudaStream_t st) {
+                                        float eps, int ctas, cudaStream_t st) {
   switch (N) {
 #define SY_RB_CASE(k) \
   case k:             \
-    return launch_reg_bat_bwd_n<T, k>(BT, D, S, rc, v, q, g, dv, dqp, P, eps, st);
+    return launch_reg_bat_bwd_n<T, k>(BT, D, S, rc, v, q, g, dv, dqp, P, eps, ctas, st);
     SY_RB_CASE(1) SY_RB_CASE(2) SY_RB_CASE(3) SY_RB_CASE(4) SY_RB_CASE(5) SY_RB_CASE(6)
     SY_RB_CASE(7) SY_RB_CASE(8) SY_RB_CASE(9)
 #undef SY_RB_CASE
@@ -387,24 +410,37 @@ static cudaError_t launch_reg_bat_bwd_t(int N, long long BT, int D, int S, int r
 // chunks, at most one chunk per thread, N <= kBwdRegMaxN, S <= 16, and its
 // shared memory within the device's opt-in limit.
 bool reg_bwd_batched_fits(int N, int D, int S, int dtype, int max_smem) {
+  return reg_bwd_batched_ctas_per_sm(N, D, S, dtype, max_smem) > 0;
+}
+
+// CTAs of the register-tile variant resident per SM (its registers allow two;
+// shared memory may allow fewer), 0 when the variant does not take the shape.
+// An SM's shared memory is the per-block opt-in limit plus the 1 KiB the
+// runtime reserves per block.
+int reg_bwd_batched_ctas_per_sm(int N, int D, int S, int dtype, int max_smem) {
   const int es = dtype == SY_F32 ? 4 : 2;
-  if (N < 1 || N > kBwdRegMaxN || S < 1 || S > kBwdBatchedMaxS || (D * es) % 16) return false;
+  if (N < 1 || N > kBwdRegMaxN || S < 1 || S > kBwdBatchedMaxS || (D * es) % 16) return 0;
   const int rc = D * es / 16;
-  if (rc > kGenericThreads) return false;
-  return reg_bwd_batched_layout(N, S, rc, 16 / es).total <= (size_t)max_smem;
+  if (rc > kGenericThreads) return 0;
+  const size_t smem = reg_bwd_batched_layout(N, S, rc, 16 / es).total;
+  if (smem > (size_t)max_smem) return 0;
+  return 2 * (smem + 1024) <= (size_t)max_smem + 1024 ? 2 : 1;
 }
 
 cudaError_t launch_reg_bwd_batched(long long BT, int N, int D, int S, int dtype, const void* v,
                                    const void* q, const void* g, void* dv, float* dq_partial,
-                                   int P, float eps, cudaStream_t st) {
+                                   int P, float eps, int ctas, cudaStream_t st) {
   const int rc = D * (dtype == SY_F32 ? 4 : 2) / 16;
   switch (dtype) {
     case SY_BF16:
-      return launch_reg_bat_bwd_t<__nv_bfloat16>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps, st);
+      return launch_reg_bat_bwd_t<__nv_bfloat16>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps,
+                                                 ctas, st);
     case SY_F16:
-      return launch_reg_bat_bwd_t<__half>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps, st);
+      return launch_reg_bat_bwd_t<__half>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps, ctas,
+                                          st);
     case SY_F32:
-      return launch_reg_bat_bwd_t<float>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps, st);
+      return launch_reg_bat_bwd_t<float>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps, ctas,
+                                         st);
     default:
       return cudaErrorInvalidValue;
   }
