@@ -122,7 +122,7 @@ def test_merge_survives_extreme_logit_separation():
 
 
 @pytest.mark.parametrize(("shape", "s"), CASES)
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_batched_backward_matches_oracle(shape, s, dtype):
     v, q, g = make(shape, s, dtype, seed=5)
     vt = v.clone().requires_grad_(True)
