@@ -30,7 +30,7 @@ import torch.distributed as dist
 from . import _native
 from .triton_op import DEFAULT_EPS, _backward, _forward, _validate
 
-__all__ = ["token_range", "exchange_dw", "block_attn_res_sharded"]
+__all__ = ["token_range", "exchange_dw", "block_attn_res_sharded", "block_attn_res_batched_sharded"]
 
 
 def token_range(bt: int, world: int, rank: int) -> tuple[int, int]:
@@ -158,3 +158,60 @@ def block_attn_res_sharded(v_local: torch.Tensor, w: torch.Tensor, eps: float = 
     same order, with the same ``w``.
     """
     return _ShardedBlockAttnRes.apply(v_local, w, eps, group)
+
+
+class _ShardedBatched(torch.autograd.Function):
+    """The batched operator on this rank's tokens; backward adds the ranks'
+    fp32 query-gradient rows ``[S*D]`` in rank order, through the same
+    exchange as ``dw`` (its length is S*D)."""
+
+    @staticmethod
+    def forward(ctx, v_local, queries, eps, group):
+        from .two_phase import _check_batched
+
+        _check_batched(v_local, queries)
+        v_local = v_local.contiguous()
+        queries = queries.contiguous()
+        n, b, t, d = v_local.shape
+        s = queries.shape[0]
+        out = torch.empty(s, b, t, d, device=v_local.device, dtype=v_local.dtype)
+        if b * t > 0:
+            with torch.cuda.device(v_local.device):
+                _native.fwd_batched(v_local, queries, out, n, b * t, d, s, eps)
+        ctx.save_for_backward(v_local, queries)
+        ctx.eps, ctx.group = eps, group
+        return out
+
+    @staticmethod
+    def backward(ctx, grad_out):
+        v, q = ctx.saved_tensors
+        n, b, t, d = v.shape
+        s = q.shape[0]
+        bt = b * t
+        g = grad_out.to(v.dtype).contiguous()
+        dv = torch.empty_like(v)
+        dq = torch.empty_like(q)
+        with torch.cuda.device(v.device):
+            p = _native.bwd_batched_partials(n, bt, d, s, v.dtype)
+            part = torch.empty(p, s * d, device=v.device, dtype=torch.float32)
+            _native.bwd_batched(v, q, g, dv, part, n, bt, d, s, ctx.eps)
+            peer = _peer_dw(ctx.group, s * d, q.device)
+            if peer is not None:
+                slot, off = peer.next_slot()
+                _native.dw_reduce(part, slot)
+                peer.exchange(off, dq.view(s * d))
+            else:
+                dq32 = torch.empty(s * d, device=v.device, dtype=torch.float32)
+                _native.dw_reduce(part, dq32)
+                dq = exchange_dw(dq32, ctx.group).to(q.dtype).view(s, d)
+        return dv, dq, None, None
+
+
+def block_attn_res_batched_sharded(v_local: torch.Tensor, queries: torch.Tensor,
+                                   eps: float = DEFAULT_EPS, group=None) -> torch.Tensor:
+    """``S`` queries against this rank's token shard ``v_local [N, B, T_local, D]``
+    (the batched training contract, ``switchyard.block_attn_res_batched_train``,
+    sharded like :func:`block_attn_res_sharded`): output and ``dv`` stay local,
+    ``queries.grad`` is the full-batch gradient, bitwise the same on every rank.
+    Every rank must call it, in the same order, with the same ``queries``."""
+    return _ShardedBatched.apply(v_local, queries, eps, group)

@@ -3,7 +3,8 @@ GPU): the peer-memory dw exchange (``sy_dw_exchange``) against the collective
 fallback and the float64 oracle.
 
 Each rank holds its contiguous token range of the same inputs; after forward +
-backward every rank must hold the bitwise-same ``dw``, equal bitwise between the
+backward every rank must hold the bitwise-same ``dw`` (and, for the batched
+training op with four queries, the same ``dq``), equal bitwise between the
 peer-memory path and the all-gather path (both add the ranks in rank order),
 stable over repeated steps (the exchange alternates its two slots), and within
 the bf16 rounding floor of the oracle's full-batch gradient. Skipped with fewer
@@ -49,7 +50,11 @@ def _worker(rank, world, port, outdir):
                             timeout=timedelta(seconds=60), device_id=dev)
     try:
         from switchyard import _native, sharding
-        from switchyard.sharding import block_attn_res_sharded, token_range
+        from switchyard.sharding import (
+            block_attn_res_batched_sharded,
+            block_attn_res_sharded,
+            token_range,
+        )
 
         g = torch.Generator().manual_seed(11)
         v = torch.randn(N, B, T, D, generator=g).to(torch.bfloat16)
@@ -70,8 +75,23 @@ def _worker(rank, world, port, outdir):
         for _ in range(3):  # three steps: both slots, then the first again
             dv, dw = step()
             dws.append(dw.clone())
+        # the batched training op on the same shard: S = 4 queries
+        qs = (torch.randn(4, D, generator=g) / D**0.5).to(torch.bfloat16)
+        gq = torch.randn(4, B, T, D, generator=g).to(torch.bfloat16)
+        gq_loc = gq.reshape(4, B * T, D)[:, lo:hi].reshape(4, 1, hi - lo, D).to(dev)
+        q_dev = qs.to(dev)
+
+        def bstep():
+            vv = v_loc.detach().requires_grad_(True)
+            qq = q_dev.detach().requires_grad_(True)
+            block_attn_res_batched_sharded(vv, qq, 1e-6).backward(gq_loc)
+            return qq.grad
+
+        dqs = [bstep().clone() for _ in range(2)]
         peer_used = bool(sharding._PEER)
         os.environ["SWITCHYARD_DW_EXCHANGE"] = "collective"
+        dqs.append(bstep().clone())
+        np.save(Path(outdir) / f"dq{rank}.npy", torch.stack(dqs).float().cpu().numpy())
         _, dw_coll = step()
         torch.cuda.synchronize()
         assert _native.device_error() == 0
@@ -115,3 +135,14 @@ def test_peer_dw_exchange_matches_collective_and_oracle(tmp_path):
     f64 = lambda t: t.to(torch.float64).numpy()  # noqa: E731
     _, dw_o = O.backward(f64(v), f64(w), f64(dout))
     assert O.rel_l2(got[0][0], dw_o) <= 1.005 * O.dtype_floor(dw_o, "bfloat16")
+
+    # batched: dq the same on every rank, peer and collective paths bitwise
+    # equal, and at the bf16 floor of the oracle's full-batch gradient
+    dq = [np.load(tmp_path / f"dq{r}.npy") for r in range(world)]
+    for r in range(world):
+        assert np.array_equal(dq[r][0], dq[r][1]) and np.array_equal(dq[r][0], dq[r][2])
+        assert np.array_equal(dq[0][0], dq[r][0])
+    qs = (torch.randn(4, D, generator=g) / D**0.5).to(torch.bfloat16)
+    gq = torch.randn(4, B, T, D, generator=g).to(torch.bfloat16)
+    _, dq_o = O.batched_backward(f64(v), f64(qs), f64(gq))
+    assert O.rel_l2(dq[0][0], dq_o) <= 1.005 * O.dtype_floor(dq_o, "bfloat16")
