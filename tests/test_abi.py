@@ -32,7 +32,8 @@ def native():
 def test_header_declares_the_entry_points():
     names = _declared()
     for required in ("sy_fwd", "sy_bwd", "sy_bwd_partials", "sy_dw_reduce", "sy_dw_reduce_gain",
-                     "sy_fwd_batched",
+                     "sy_fwd_batched", "sy_fwd_batched_stats", "sy_bwd_batched",
+                     "sy_bwd_batched_partials", "sy_merge_stats", "sy_stage_partial",
                      "sy_speed_of_light", "sy_stats_stride", "sy_status_string"):
         assert required in names
 
@@ -95,6 +96,29 @@ def test_host_validation_rejects_bad_arguments(native):
     assert L.sy_dw_reduce_gain(1, 0, 8, 1, 1, 1, 1, bf16, None) == native.SY_ERR_ARG
     assert L.sy_dw_reduce_gain(1, 4, 8, 1, 1, None, None, bf16, None) == native.SY_OK
     assert L.sy_dw_reduce_gain(None, 4, 0, None, None, 1, 1, bf16, None) == native.SY_OK
+    # batched forward with merge statistics: dtype, S, raw flag, null statistics, empty
+    assert L.sy_fwd_batched_stats(1, 1, 1, 8, 0, 2, 4, 8, 2, bad, 1e-6, None) == native.SY_ERR_DTYPE
+    assert L.sy_fwd_batched_stats(1, 1, 1, 8, 0, 2, 4, 8, 0, bf16, 1e-6, None) == native.SY_ERR_ARG
+    assert L.sy_fwd_batched_stats(1, 1, 1, 8, 2, 2, 4, 8, 2, bf16, 1e-6, None) == native.SY_ERR_ARG
+    assert L.sy_fwd_batched_stats(1, 1, 1, None, 1, 2, 4, 8, 2, bf16, 1e-6, None) == native.SY_ERR_ARG
+    assert L.sy_fwd_batched_stats(None, None, None, None, 0, 2, 0, 8, 2, bf16, 1e-6, None) == native.SY_OK
+    # batched backward: partial-row count, dtype, S, empty problems
+    assert L.sy_bwd_batched_partials(0, 4, 8, 2, bf16) < 0
+    assert L.sy_bwd_batched_partials(3, 0, 8, 2, bf16) == 1
+    assert L.sy_bwd_batched(1, 1, 1, 1, 1, 1, 3, 4, 8, 2, bad, 1e-6, None) == native.SY_ERR_DTYPE
+    assert L.sy_bwd_batched(1, 1, 1, 1, 1, 1, 3, 4, 8, 0, bf16, 1e-6, None) == native.SY_ERR_ARG
+    assert L.sy_bwd_batched(None, None, None, None, None, 1, 3, 0, 0, 2, bf16, 1e-6, None) == native.SY_OK
+    # merge: dtype, normalize flag, null inputs, misaligned statistics, no rows
+    assert L.sy_merge_stats(8, 8, 8, 8, 8, 8, 0, 4, 8, bad, None) == native.SY_ERR_DTYPE
+    assert L.sy_merge_stats(8, 8, 8, 8, 8, 8, 2, 4, 8, bf16, None) == native.SY_ERR_ARG
+    assert L.sy_merge_stats(8, None, 8, 8, 8, 8, 0, 4, 8, bf16, None) == native.SY_ERR_ARG
+    assert L.sy_merge_stats(8, 4, 8, 8, 8, 8, 0, 4, 8, bf16, None) == native.SY_ERR_ARG
+    assert L.sy_merge_stats(None, None, None, None, None, None, 1, 0, 8, bf16, None) == native.SY_OK
+    # arena staging: dtype, negative length, null buffers, empty
+    assert L.sy_stage_partial(1, 1, 1, 1, 8, bad, None) == native.SY_ERR_DTYPE
+    assert L.sy_stage_partial(1, 1, 1, 1, -1, bf16, None) == native.SY_ERR_ARG
+    assert L.sy_stage_partial(1, None, 1, 1, 8, bf16, None) == native.SY_ERR_ARG
+    assert L.sy_stage_partial(None, None, None, None, 0, bf16, None) == native.SY_OK
 
 
 B200 = dict(sms=148, max_smem=232448)  # multiprocessors, opt-in shared memory per block
