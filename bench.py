@@ -19,15 +19,19 @@ and the SM clocks sampled (NVML) during the timed region.
 
 ``--gpus N`` (under torchrun): each rank runs the same shape on its own token
 shard (weak scaling); the step's only exchange is the fp32 dw sum of
-``switchyard.sharding``: peer-memory copies added in rank order by one kernel
-(``sy_dw_exchange``), no NCCL on the step.
+``switchyard.sharding``: one kernel (``sy_dw_exchange``) reduces the rank's
+partial rows and adds all ranks' rows over NVLink peer loads in rank order, no
+NCCL on the step. Each timed step starts after a device-side barrier across the
+ranks' streams, so no rank's events hold another rank's flush or host jitter;
+the line also carries each rank's mean, the exchange kernel timed alone, and
+the exchange's own flag-wait time read from device counters.
 
 ``--sweep``: forward, backward and step times for bf16, fp16 and fp32 at a few
 shapes (one JSON line each; no bench line).
 
 ``--impl reference``: the reference's PyTorch eager CPU path (restated in
 ``oracle/eager_port.py``; the reference itself cannot run on the GPU box),
-fwd+bwd on a bounded token sample on all host threads; rank 0 only.
+fwd+bwd of the whole workload on all host threads; rank 0 only.
 """
 
 from __future__ import annotations
@@ -55,7 +59,6 @@ REP = (9, 1, 4096, 2048)
 ITEM = 2  # bf16
 FLUSH_BYTES = 384 * 2**20
 FALLBACK_HBM_GBS = 6650.0
-CPU_SAMPLE_T = 256  # tokens per CPU-baseline step (bounded sample of the workload)
 
 
 # ----------------------------------------------------------------------------- setup
@@ -76,6 +79,12 @@ def parse_args():
                          "shape, for an ncu capture; prints nothing")
     ap.add_argument("--shape", default=None,
                     help="N,B,T,D for --profile (default: the representative shape)")
+    ap.add_argument("--decoder", action="store_true",
+                    help="no bench line: the 1.3B Block AttnRes decoder (BASELINE config 5), a bf16 "
+                         "AdamW training step of the standard and the switchyard residual at B=4 "
+                         "T=2048 per GPU, DDP over NCCL under torchrun; one JSON line")
+    ap.add_argument("--decoder-batch", type=int, default=4)
+    ap.add_argument("--decoder-seq", type=int, default=2048)
     ap.add_argument("--sweep", action="store_true",
                     help="no bench line: time forward, backward and the fwd+bwd step through the "
                          "C ABI for bf16, fp16 and fp32 at a few shapes, one JSON line each")
@@ -208,15 +217,20 @@ class L2Flush:
         torch.sum(self.r, dim=0, out=self.o)
 
 
-def timed_steps(fn, steps, flush, lead_cycles=2_000_000):
+def timed_steps(fn, steps, flush, lead_cycles=2_000_000, align=None):
     """Per-step device times (ms): flush L2, let a spin kernel cover the host's
     queueing of the step, then bracket only the step with CUDA events on the
-    current stream."""
+    current stream. ``align`` (multi-GPU) queues a device-side barrier across
+    the ranks' streams after the spin kernel, so every rank's step starts at
+    the same moment and no rank's events include another rank's flush or
+    host jitter."""
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for i in range(steps):
         flush()
         torch.cuda._sleep(lead_cycles)
+        if align is not None:
+            align()
         starts[i].record()
         fn()
         ends[i].record()
@@ -253,35 +267,70 @@ def make_inputs(dev, rank, n, b, t, d, dtype=torch.bfloat16):
     return v, w, dout
 
 
-def cpu_baseline(seconds: float):
-    """The reference's eager CPU path (restated in oracle/eager_port.py),
-    fwd+bwd, on a bounded sample of the workload: T=256 of the 4096 tokens."""
-    from oracle.eager_port import fwd_bwd
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
 
-    n, b, _, d = REP
-    t = CPU_SAMPLE_T
+
+def cpu_time(n, b, t, d, dtype, seconds, min_reps=3, fwd_only=False):
+    """Median seconds of one reference eager CPU call (oracle/eager_port.py,
+    the reference's operator sequence): forward + backward through autograd,
+    or the forward alone. Synthetic inputs as the bench's."""
+    from oracle.eager_port import block_attn_res_eager, fwd_bwd
+
     gen = torch.Generator().manual_seed(0)
-    v = torch.randn(n, b, t, d, generator=gen).to(torch.bfloat16)
-    w = (torch.randn(d, generator=gen) / math.sqrt(d)).to(torch.bfloat16)
-    g = torch.randn(b, t, d, generator=gen).to(torch.bfloat16)
-    fwd_bwd(v, w, g)
+    v = torch.randn(n, b, t, d, generator=gen).to(dtype)
+    w = (torch.randn(d, generator=gen) / math.sqrt(d)).to(dtype)
+    g = torch.randn(b, t, d, generator=gen).to(dtype)
+
+    def call():
+        if fwd_only:
+            with torch.no_grad():
+                block_attn_res_eager(v, w)
+        else:
+            fwd_bwd(v, w, g)
+
+    call()
     times = []
     t_end = time.perf_counter() + seconds
-    while len(times) < 3 or time.perf_counter() < t_end:
+    while len(times) < min_reps or time.perf_counter() < t_end:
         t0 = time.perf_counter()
-        fwd_bwd(v, w, g)
+        call()
         times.append(time.perf_counter() - t0)
-    per = statistics.median(times)
+    return statistics.median(times), len(times)
+
+
+def cpu_baseline(seconds: float):
+    """The reference's eager CPU path (restated in oracle/eager_port.py) on the
+    bench's own workload, N=9 B=1 T=4096 D=2048 bf16, forward + backward, on
+    all host threads; beside it the same in fp32, the forward alone, and
+    BASELINE config 1 (N=4 B=1 T=256 D=512 fp32)."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    n, b, t, d = REP
+    per, reps = cpu_time(n, b, t, d, torch.bfloat16, seconds)
+    fwd_s, _ = cpu_time(n, b, t, d, torch.bfloat16, seconds / 4, fwd_only=True)
+    f32, _ = cpu_time(n, b, t, d, torch.float32, seconds / 2)
+    c1, _ = cpu_time(4, 1, 256, 512, torch.float32, 2.0)
     _, _, tot = alg_bytes(n, b, t, d)
     return {
         "value": tot / per / 1e12,
         "unit": "TB/s",
         "cores": torch.get_num_threads(),
         "kind": "port",
-        "sample": f"fwd+bwd of the reference eager path (oracle/eager_port.py) on N={n} B={b} T={t} D={d} bf16 "
-                  f"(T={t} of 4096 tokens), median of {len(times)} runs, {per * 1e3:.1f} ms each",
-        "ms_per_sample": per * 1e3,
+        "sample": f"the whole workload: fwd+bwd of the reference eager path (oracle/eager_port.py) at "
+                  f"N={n} B={b} T={t} D={d} bf16, median of {reps} runs, {per * 1e3:.1f} ms each",
+        "same_config": True,
+        "ms_per_step": per * 1e3,
+        "fwd_ms": fwd_s * 1e3,
+        "fp32_ms_per_step": f32 * 1e3,
+        "config1_fp32_ms_per_step": c1 * 1e3,
         "cpu_count": os.cpu_count(),
+        "cpu_model": cpu_model(),
     }
 
 
@@ -457,40 +506,113 @@ def stage_times(v, steps, flush, hbm_gbs):
 
 
 def e2e_times(dev, steps, n, b, t, d, op):
-    """Same step through the public API from pinned host buffers: H2D of v, w
-    and dout, forward + backward, D2H of dw -- all inside the events."""
+    """The step through the public API from pinned host buffers, every step:
+    H2D of v, w and dout, forward + backward (block_attn_res_triton), and D2H
+    of the results out, dv and dw -- all inside the events.
+
+    ``serial``: each step alone (copy in, compute, copy out, one after the
+    other). ``pipelined``: the same K steps with the next step's H2D on a copy
+    stream and the previous step's D2H on another, overlapping the compute (two
+    device buffer sets; PCIe carries the two directions at once); the time is
+    from before the first H2D to after the last D2H, divided by K."""
     gen = torch.Generator().manual_seed(3)
     v_h = torch.randn(n, b, t, d, generator=gen).to(torch.bfloat16).pin_memory()
     w_h = (torch.randn(d, generator=gen) / math.sqrt(d)).to(torch.bfloat16).pin_memory()
     g_h = torch.randn(b, t, d, generator=gen).to(torch.bfloat16).pin_memory()
-    dw_h = torch.empty(d, dtype=torch.bfloat16).pin_memory()
+    outs_h = [(torch.empty(b, t, d, dtype=torch.bfloat16).pin_memory(),
+               torch.empty(n, b, t, d, dtype=torch.bfloat16).pin_memory(),
+               torch.empty(d, dtype=torch.bfloat16).pin_memory()) for _ in range(2)]
+    ins_d = [(torch.empty(n, b, t, d, dtype=torch.bfloat16, device=dev),
+              torch.empty(d, dtype=torch.bfloat16, device=dev),
+              torch.empty(b, t, d, dtype=torch.bfloat16, device=dev)) for _ in range(2)]
+    h2d = v_h.numel() * 2 + w_h.numel() * 2 + g_h.numel() * 2
+    d2h = sum(x.numel() * 2 for x in outs_h[0])
 
-    def step():
-        v = v_h.to(dev, non_blocking=True).requires_grad_(True)
-        w = w_h.to(dev, non_blocking=True).requires_grad_(True)
-        g = g_h.to(dev, non_blocking=True)
-        op(v, w).backward(g)
-        dw_h.copy_(w.grad, non_blocking=True)
+    def compute(k):
+        vd, wd, gd = ins_d[k]
+        vv = vd.detach().requires_grad_(True)
+        ww = wd.detach().requires_grad_(True)
+        out = op(vv, ww)
+        out.backward(gd)
+        return out.detach(), vv.grad, ww.grad
+
+    def serial_step():
+        vd, wd, gd = ins_d[0]
+        vd.copy_(v_h, non_blocking=True)
+        wd.copy_(w_h, non_blocking=True)
+        gd.copy_(g_h, non_blocking=True)
+        for dst, src in zip(outs_h[0], compute(0)):
+            dst.copy_(src, non_blocking=True)
 
     for _ in range(3):
-        step()
+        serial_step()
     torch.cuda.synchronize()
     ms = []
     for _ in range(steps):
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        step()
-        e.record()
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record()
+        serial_step()
+        e_.record()
         torch.cuda.synchronize()
-        ms.append(s.elapsed_time(e))
-    h2d = v_h.numel() * 2 + w_h.numel() * 2 + g_h.numel() * 2
-    return summarize(ms), h2d, dw_h.numel() * 2
+        ms.append(s_.elapsed_time(e_))
+
+    main = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+
+    def pipelined(k_steps):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        loaded = [torch.cuda.Event() for _ in range(k_steps)]
+        consumed = [torch.cuda.Event() for _ in range(k_steps)]
+        start.record(main)
+        up.wait_event(start)
+        down.wait_event(start)
+        for i in range(k_steps):
+            k = i & 1
+            with torch.cuda.stream(up):
+                if i >= 2:
+                    up.wait_event(consumed[i - 2])  # compute of step i-2 is done with set k
+                for dst, src in zip(ins_d[k], (v_h, w_h, g_h)):
+                    dst.copy_(src, non_blocking=True)
+                loaded[i].record(up)
+            main.wait_event(loaded[i])
+            res = compute(k)
+            consumed[i].record(main)
+            down.wait_event(consumed[i])
+            with torch.cuda.stream(down):
+                for dst, src in zip(outs_h[k], res):
+                    src.record_stream(down)
+                    dst.copy_(src, non_blocking=True)
+        main.wait_stream(down)
+        end.record(main)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / k_steps
+
+    pipelined(3)
+    pipe_ms = pipelined(steps)
+    return summarize(ms), pipe_ms, h2d, d2h
+
+
+def exchange_alone(peer, part, dw, steps, align):
+    """Device time of the fused partial-row reduction + peer exchange alone
+    (sy_dw_exchange), each call after a device barrier across the ranks, with
+    the backward's real partial rows. Returns this rank's mean in ms."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        torch.cuda._sleep(200_000)
+        align()
+        starts[i].record()
+        peer.reduce_exchange(part, dw)
+        ends[i].record()
+    torch.cuda.synchronize()
+    return statistics.fmean(s_.elapsed_time(e_) for s_, e_ in zip(starts, ends))
 
 
 def run_ours(args):
     import torch.distributed as dist
 
     from switchyard import _native, block_attn_res_triton, speed_of_light  # noqa: F401
+    from switchyard import sharding
     from switchyard.sharding import block_attn_res_sharded
 
     rank, world, local = dist_env()
@@ -507,6 +629,7 @@ def run_ours(args):
     v, w, dout = make_inputs(dev, rank, n, b, t, d)
     flush = L2Flush(dev)
     op = block_attn_res_triton if world == 1 else block_attn_res_sharded
+    align = (lambda: sharding.device_barrier(None, dev)) if world > 1 else None
 
     def step():
         vv = v.detach().requires_grad_(True)
@@ -520,28 +643,91 @@ def run_ours(args):
     for _ in range(max(args.warmup, 3)):
         step()
         fwd_only()
+        if align is not None:
+            align()
     torch.cuda.synchronize()
+    peer = sharding.peer_exchange(None, d, dev) if world > 1 else None
 
     sampler = ClockSampler(local)
     if world > 1:
         dist.barrier()
+        peer.start_timing()
     torch.cuda.synchronize()
     with sampler:
-        step_ms = timed_steps(step, args.steps, flush)
+        step_ms = timed_steps(step, args.steps, flush, align=align)
     torch.cuda.synchronize()
+    exch = None
     if world > 1:
+        exch = peer.read_timing()
         dist.barrier()
-    fwd_ms = timed_steps(fwd_only, args.steps, flush)
+    fwd_ms = timed_steps(fwd_only, args.steps, flush, align=align)
 
     st_step, st_fwd = summarize(step_ms), summarize(fwd_ms)
     mean_step, mean_fwd = st_step["mean_ms"], st_fwd["mean_ms"]
+    per_rank = None
     if world > 1:
-        tt = torch.tensor([mean_step, mean_fwd], device=dev, dtype=torch.float64)
-        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
-        mean_step, mean_fwd = tt.tolist()
+        # the same step timed without the per-step device barrier (the ranks
+        # then start each step after their own flush, so each rank's events
+        # also hold the other ranks' skew): reported beside the aligned number
+        unaligned = summarize(timed_steps(step, args.steps, flush))
+        # the exchange kernel alone, with the backward's own partial rows
+        from switchyard.triton_op import _backward_partials, _forward
+
+        stats = _forward(v, w, 1e-6)[3]
+        _, part = _backward_partials(v, w, stats, dout, 1e-6)
+        dw_ = torch.empty_like(w)
+        ex_ms = exchange_alone(peer, part, dw_, max(20, args.steps), align)
+        mine = torch.tensor([mean_step, mean_fwd, unaligned["mean_ms"], ex_ms,
+                             exch["wait_mean_us"], exch["wait_max_us"], exch["kernel_mean_us"],
+                             exch["reduce_mean_us"], exch["announce_mean_us"],
+                             exch["peer_sum_mean_us"]],
+                            device=dev, dtype=torch.float64)
+        allr = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(allr, mine)
+        allr = torch.stack(allr).tolist()
+        mean_step = max(r[0] for r in allr)
+        mean_fwd = max(r[1] for r in allr)
+        per_rank = {
+            "step_ms": [r[0] for r in allr],
+            "fwd_ms": [r[1] for r in allr],
+            "step_unaligned_ms": [r[2] for r in allr],
+            "exchange_kernel_alone_us": [r[3] * 1e3 for r in allr],
+            "exchange_flag_wait_mean_us": [r[4] for r in allr],
+            "exchange_flag_wait_max_us": [r[5] for r in allr],
+            "exchange_kernel_in_step_mean_us": [r[6] for r in allr],
+            "exchange_phase_partial_sum_us": [r[7] for r in allr],
+            "exchange_phase_announce_us": [r[8] for r in allr],
+            "exchange_phase_peer_sum_us": [r[9] for r in allr],
+        }
 
     fwd_b, bwd_b, tot_b = alg_bytes(n, b, t, d)
     peak, peak_kind = load_peaks()
+    e2e = None
+    if not args.no_extras:
+        # every rank (the sharded op's backward exchanges dw with all of them)
+        if world > 1:
+            dist.barrier()
+        e2e_serial, pipe_ms, h2d, d2h = e2e_times(dev, 10, n, b, t, d, op)
+        pipe_max, serial_max = pipe_ms, e2e_serial["mean_ms"]
+        if world > 1:
+            tt = torch.tensor([pipe_ms, serial_max], device=dev, dtype=torch.float64)
+            dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+            pipe_max, serial_max = tt.tolist()
+        e2e = {
+            "value": world * tot_b / (pipe_max * 1e-3) / 1e12,
+            "unit": "TB/s",
+            "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h,
+            "ms_per_step": pipe_max,
+            "serial_ms_per_step": serial_max,
+            "serial_value": world * tot_b / (serial_max * 1e-3) / 1e12,
+            "api": ("switchyard.block_attn_res_triton" if world == 1 else
+                    "switchyard.sharding.block_attn_res_sharded") +
+                   " (autograd) from pinned host buffers on every rank: H2D of v, w, dout and D2H "
+                   "of out, dv, dw every step (bytes per rank); value: the next step's H2D and the "
+                   "previous step's D2H overlap the compute on two copy streams (serial_*: one "
+                   "step at a time); max over ranks",
+        }
     result = None
     if rank == 0:
         kt, p_rows = kernel_times(_native, v, w, dout, args.steps, flush, None)
@@ -569,6 +755,11 @@ def run_ours(args):
                 "l2": "flushed before every timed step, outside its events: 384 MiB written, "
                       "then 256 MiB of another buffer read (no dirty flush lines left in L2)",
                 "parallelism": f"token-axis shards x{world}" if world > 1 else "single GPU",
+                "timing": ("per step: L2 flush, spin kernel, device-side barrier across the ranks' "
+                           "streams (sy_dw_exchange on one value), then CUDA events around the "
+                           "step on every rank; value uses the max over ranks of the mean"
+                           if world > 1 else
+                           "per step: L2 flush, spin kernel, then CUDA events around the step"),
             },
             "fwd_us": mean_fwd * 1e3,
             "fwd_bwd_us": mean_step * 1e3,
@@ -602,27 +793,24 @@ def run_ours(args):
             },
             "kernels_ms": {k: v_["mean_ms"] for k, v_ in kt.items()},
             "dw_partial_rows": p_rows,
-            # per step: forward, backward, dw reduction (+ the peer dw exchange on N > 1)
+            # per step: forward, backward, and the dw reduction -- fused with the
+            # peer exchange on N > 1 (sy_dw_exchange); on N > 1 also the per-step
+            # device barrier (outside each step's events)
             "gpu_launches": (3 if world == 1 else 4) * args.steps,
             "clocks": sampler.summary(),
         }
+        if per_rank is not None:
+            result["per_rank"] = per_rank
     if not args.no_extras and rank == 0:
         result["batched"] = batched_times(v, max(20, args.steps // 4), flush, peak)
         result["batched_train"] = batched_train_times(v, max(10, args.steps // 10), flush, peak)
         result["arena_stage"] = stage_times(v, max(20, args.steps // 4), flush, peak)
-        e2e, h2d, d2h = e2e_times(dev, 10, n, b, t, d, block_attn_res_triton)
-        result["e2e"] = {
-            "value": tot_b / (e2e["mean_ms"] * 1e-3) / 1e12,
-            "unit": "TB/s",
-            "h2d_bytes_per_step": h2d,
-            "d2h_bytes_per_step": d2h,
-            "ms_per_step": e2e["mean_ms"],
-            "api": "switchyard.block_attn_res_triton (autograd) from pinned host buffers, rank 0",
-        }
+        result["e2e"] = e2e
     if rank == 0 and world == 1:
         result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
     if world > 1:
         dist.barrier()
+        sharding._PEER.clear()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result), flush=True)
@@ -676,14 +864,17 @@ def read_traffic():
 
 
 def run_reference(args):
+    """The reference's PyTorch eager CPU path (restated in oracle/eager_port.py:
+    the reference's own package cannot travel to the GPU box) on the bench's
+    own workload -- N=9 B=1 T=4096 D=2048 bf16, forward + backward through
+    autograd -- on all host threads; rank 0 only."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
     from oracle.eager_port import fwd_bwd
 
     torch.set_num_threads(os.cpu_count() or 1)
-    n, b, _, d = REP
-    t = CPU_SAMPLE_T
+    n, b, t, d = REP
     gen = torch.Generator().manual_seed(0)
     v = torch.randn(n, b, t, d, generator=gen).to(torch.bfloat16)
     w = (torch.randn(d, generator=gen) / math.sqrt(d)).to(torch.bfloat16)
@@ -698,8 +889,8 @@ def run_reference(args):
     mean = statistics.fmean(times)
     _, _, tot = alg_bytes(n, b, t, d)
     value = tot / mean / 1e12
-    sample = (f"reference eager fwd+bwd (oracle/eager_port.py) on N={n} B={b} T={t} D={d} bf16, "
-              f"T={t} of the 4096 tokens per step")
+    sample = (f"the whole workload each step: reference eager fwd+bwd (oracle/eager_port.py) at "
+              f"N={n} B={b} T={t} D={d} bf16, {torch.get_num_threads()} threads of {cpu_model()}")
     print(json.dumps({
         "impl": "reference",
         "metric": METRIC,
@@ -715,9 +906,10 @@ def run_reference(args):
         "dtype": "bf16",
         "data": "synthetic: v~N(0,1), w~N(0,1/D), dout~N(0,1)",
         "config": {"workload": "Block AttnRes forward+backward, reference PyTorch eager on CPU",
-                   "N": n, "B": b, "T": t, "D": d, "sampled_from_T": REP[2]},
+                   "N": n, "B": b, "T": t, "D": d},
         "cpu_baseline": {"value": value, "unit": "TB/s", "cores": torch.get_num_threads(),
-                         "kind": "port", "sample": sample},
+                         "kind": "port", "sample": sample, "same_config": True,
+                         "cpu_count": os.cpu_count(), "cpu_model": cpu_model()},
         "e2e": {"value": value, "unit": "TB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -769,6 +961,140 @@ def run_sweep(args):
             print(json.dumps(line), flush=True)
             del v, dout, dv, out, part
             torch.cuda.empty_cache()
+
+
+def run_decoder(args):
+    """the 1.3B decoder (switchyard.decoder, 24 layers, hidden
+    2048, 16 heads, SwiGLU 5632, 8 blocks, vocabulary 32000, N(0, 0.02) init)
+    trained in bf16 with AdamW on synthetic tokens uniform over the vocabulary,
+    B x T tokens per GPU, for the standard residual and for Block AttnRes on
+    this package's kernels (arena sources). Under torchrun the model is wrapped
+    in DistributedDataParallel: NCCL all-reduces the gradient buckets during
+    the backward, the only collective (the operator itself needs none). The
+    pattern of the reference's bench/bench_ddp.py:40-126, for any world size.
+
+    Per mode: the step's device time (CUDA events around each step, mean, max
+    over ranks) and global tokens/s; at N > 1 also the same step without the
+    gradient all-reduce (DDP no_sync) -- the difference is the all-reduce's
+    exposed share of the step -- an all-reduce of one flat buffer of the
+    model's gradient size on its own, and the rank-gradient check: every
+    rank's gradients after a synchronised backward against rank 0's
+    (broadcast), max abs deviation."""
+    import torch.distributed as dist
+    from torch.nn.parallel import DistributedDataParallel
+
+    from switchyard.decoder import Decoder, DecoderConfig
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    b, t = args.decoder_batch, args.decoder_seq
+    steps, warmup = max(args.steps, 1), max(args.warmup, 3)
+    results = {}
+    for residual in ("standard", "switchyard"):
+        cfg = DecoderConfig(residual=residual, sources="arena")
+        torch.manual_seed(0)
+        with torch.device(dev):
+            model = Decoder(cfg)
+        model = model.to(torch.bfloat16)
+        n_params = sum(p.numel() for p in model.parameters())
+        net = DistributedDataParallel(model, device_ids=[local]) if world > 1 else model
+        opt = torch.optim.AdamW(net.parameters(), lr=1e-6)
+        gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+        idx = torch.randint(0, cfg.vocab_size, (b, t), device=dev, generator=gen)
+        tgt = torch.randint(0, cfg.vocab_size, (b, t), device=dev, generator=gen)
+
+        def step(sync=True):
+            opt.zero_grad(set_to_none=True)
+            if sync or world == 1:
+                net(idx, tgt)[1].backward()
+            else:
+                with net.no_sync():
+                    net(idx, tgt)[1].backward()
+            opt.step()
+
+        def timed(sync=True):
+            for _ in range(warmup):
+                step(sync)
+            torch.cuda.synchronize()
+            if world > 1:
+                dist.barrier()
+            ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(steps)]
+            for s_, e_ in ev:
+                s_.record()
+                step(sync)
+                e_.record()
+            torch.cuda.synchronize()
+            ms = statistics.fmean(s_.elapsed_time(e_) for s_, e_ in ev)
+            if world > 1:
+                tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                ms = tt.item()
+            return ms
+
+        torch.cuda.reset_peak_memory_stats(dev)
+        ms = timed(True)
+        res = {"step_ms": ms, "tokens_per_s": world * b * t / (ms * 1e-3), "params": n_params,
+               "peak_memory_gib": torch.cuda.max_memory_allocated(dev) / 2**30}
+        if world > 1:
+            ms_local = timed(False)
+            res["step_no_allreduce_ms"] = ms_local
+            res["allreduce_exposed_ms"] = ms - ms_local
+            res["allreduce_exposed_share"] = (ms - ms_local) / ms
+            opt.zero_grad(set_to_none=True)
+            net(idx, tgt)[1].backward()
+            flat = torch.cat([p.grad.flatten().float() for _, p in sorted(model.named_parameters())
+                              if p.grad is not None])
+            other = flat.clone()
+            dist.broadcast(other, src=0)
+            res["max_abs_grad_deviation_from_rank0"] = (flat - other).abs().max().item()
+            dev_all = torch.tensor([res["max_abs_grad_deviation_from_rank0"]], device=dev)
+            dist.all_reduce(dev_all, op=dist.ReduceOp.MAX)
+            res["max_abs_grad_deviation_from_rank0"] = dev_all.item()
+            res["grad_norm"] = flat.norm().item()
+            del flat, other
+            opt.zero_grad(set_to_none=True)
+        results[residual] = res
+        del net, model, opt
+        torch.cuda.empty_cache()
+    if world > 1:
+        # the gradient all-reduce alone: one flat bf16 buffer of the model's size
+        buf = torch.ones(results["switchyard"]["params"], dtype=torch.bfloat16, device=dev)
+        for _ in range(2):
+            dist.all_reduce(buf)
+        torch.cuda.synchronize()
+        dist.barrier()
+        s_, e_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s_.record()
+        for _ in range(5):
+            dist.all_reduce(buf)
+        e_.record()
+        torch.cuda.synchronize()
+        ar_ms = s_.elapsed_time(e_) / 5
+        nbytes = buf.numel() * 2
+        results["allreduce_alone"] = {"bytes": nbytes, "ms": ar_ms,
+                                      "bus_gbs": 2 * (world - 1) / world * nbytes / (ar_ms * 1e-3) / 1e9}
+        del buf
+    if rank == 0:
+        print(json.dumps({
+            "metric": "1.3B Block AttnRes decoder bf16 training step (ms, tokens/s)",
+            "n_gpus": world, "steps": steps, "warmup": warmup,
+            "config": {"workload": "switchyard.decoder.Decoder 1.3B (24 layers, hidden 2048, 16 heads, "
+                                   "SwiGLU 5632, 8 blocks, vocab 32000), AdamW lr 1e-6, bf16",
+                       "batch_per_gpu": b, "seq_len": t,
+                       "parallelism": f"DDP x{world} (NCCL gradient all-reduce)" if world > 1
+                       else "single GPU"},
+            "data": "synthetic tokens uniform over the vocabulary, seed 1234 + rank",
+            "results": results,
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_profile(kind: str, shape: str | None = None):
@@ -826,6 +1152,9 @@ def main():
         return
     if args.sweep:
         run_sweep(args)
+        return
+    if args.decoder:
+        run_decoder(args)
         return
     if args.impl == "reference":
         run_reference(args)

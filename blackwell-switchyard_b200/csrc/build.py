@@ -97,17 +97,17 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False,
         cmds.append([nvcc, *ARCH, *FLAGS, *dflags, "-Xptxas", "-v", "-dc", str(src), "-o", str(obj)])
     jobs = jobs or min(len(cmds), os.cpu_count() or 4)
     with cf.ThreadPoolExecutor(max_workers=jobs) as ex:
-        for cmd, rc, out in ex.map(_run, cmds):
+        for cmd, rc, log in ex.map(_run, cmds):
             if verbose:
-                print(out)
+                print(log)
             if rc != 0:
-                raise RuntimeError(f"nvcc failed ({rc}): {' '.join(cmd)}\n{out}")
-            (bdir / (Path(cmd[-3]).stem + ".ptxas.txt")).write_text(out)
+                raise RuntimeError(f"nvcc failed ({rc}): {' '.join(cmd)}\n{log}")
+            (bdir / (Path(cmd[-3]).stem + ".ptxas.txt")).write_text(log)
     tmp = lib.with_suffix(".so.tmp")
     link = [nvcc, *ARCH, "-rdc=true", "-shared", "-cudart", "shared", *map(str, objs), "-o", str(tmp)]
-    cmd, rc, out = _run(link)
+    cmd, rc, log = _run(link)
     if rc != 0:
-        raise RuntimeError(f"link failed ({rc}): {' '.join(cmd)}\n{out}")
+        raise RuntimeError(f"link failed ({rc}): {' '.join(cmd)}\n{log}")
     os.replace(tmp, lib)
     if out is None and not defines:
         STAMP.write_text(_digest() + "\n")

@@ -37,6 +37,27 @@ __device__ __forceinline__ void record_device_error(unsigned flag) {
   atomicOr(&g_device_error, flag);
 }
 
+// Warp `wp`'s share (of 8 warps) of the fixed-order sum of the fp32 partial
+// rows part[P, L] at column `col`: rows wp, wp + 8, wp + 16, ... added in
+// increasing order, 32 loads in flight per batch. The dw reduction adds the 8
+// warp shares in warp order after it; every kernel that reduces partial rows
+// uses this so their results agree bitwise.
+__device__ __forceinline__ float partial_rows_warp_sum(const float* __restrict__ part, long long P,
+                                                       long long L, long long col, int wp) {
+  float acc = 0.f;
+  for (long long p0 = wp; p0 < P; p0 += 8 * 32) {
+    float x[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const long long p = p0 + 8 * i;
+      x[i] = p < P ? __ldcs(part + p * L + col) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc += x[i];
+  }
+  return acc;
+}
+
 // ---------------------------------------------------------------------------
 // dtype traits
 // ---------------------------------------------------------------------------

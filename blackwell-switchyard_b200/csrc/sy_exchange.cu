@@ -1,27 +1,43 @@
-// sy_exchange.cu -- the cross-GPU dw sum of token-sharded training.
+// sy_exchange.cu -- the cross-GPU dw sum of token-sharded training, fused with
+// the fixed-order reduction of the backward's partial rows.
 //
-// With the token axis split across ranks, every rank's backward produces an
-// fp32 dw over its own tokens; the full-batch dw is their sum. Each rank keeps
-// two fp32 slots of D floats and an array of `world` uint32 flags in memory
-// that every peer can address (NVLink peer mappings; the host side sets them up
-// and passes each rank's base address). One call, on every rank, with the
-// rank's own dw already written into slot `tag & 1` by an earlier kernel on the
-// same stream:
+// With the token axis split across ranks, every rank's backward leaves P fp32
+// partial rows of length L (L = D for the single-query operator, S*D for the
+// batched one); the full-batch gradient is the sum over all ranks of the sum
+// of their rows. Each rank owns a buffer that every peer can address (NVLink
+// peer mappings, set up by the host) holding two fp32 slots of L floats and
+// world * nblk uint32 flags, nblk = ceil(L / 32): one flag per (source rank,
+// 32-column block). One launch per rank, as a programmatic dependent of the
+// backward, does for every 32-column block b:
 //
-//   1. announce: store `tag` into flag[rank] of every rank (release, system
-//      scope, after a system fence), i.e. "my slot for this tag is complete";
-//   2. wait until this rank's own flag array holds `tag` for every rank
-//      (acquire loads, bounded by a 2 s limit that records the device error word
-//      instead of hanging);
-//   3. read all ranks' slots with plain peer loads and add them in rank order
-//      0..world-1 (so every rank gets the bitwise-same result), writing dw in
-//      the requested dtype.
+//   1. sum the P partial rows of the block's columns in the fixed order of
+//      sy_dw_reduce (8 warps, warp w taking rows w, w+8, ..., then the 8 warp
+//      sums in warp order), so the rank's own row is bitwise sy_dw_reduce's;
+//   2. store it into the rank's own slot `tag & 1`, then announce: store `tag`
+//      into flag[rank][b] of every rank (system-scope fence, release store);
+//   3. wait until this rank's flags [r][b] hold `tag` for every rank r
+//      (acquire loads, bounded by `wait_limit_ns`: on timeout the block's
+//      output is NaN, the device error word gets kDevErrWaitTimeout and the
+//      optional fail word gets the tag -- nothing hangs);
+//   4. add the ranks' slot columns in rank order 0..world-1 (the own one from
+//      registers, the others with plain peer loads) and write the result in
+//      the output dtype: bitwise the same on every rank, and bitwise the sum an
+//      all-gather of the ranks' sy_dw_reduce rows followed by a rank-order fp32
+//      sum gives.
 //
-// Slots alternate by tag parity: a rank reuses a slot two calls later, and by
-// then every peer has announced the next tag, which it only does after its own
-// reads of the previous one finished (stream order) -- so no slot is rewritten
-// while a peer may still read it. Tags increase by one per call and are
-// compared modulo 2^32.
+// Every block only waits on the same block of its peers, and the grid is
+// small enough to be resident at once (a grid-stride loop covers larger L),
+// so no CTA waits on a CTA of its own GPU that has not been scheduled.
+//
+// Slots alternate by tag parity: a rank rewrites a slot two calls later, and by
+// then every peer has announced the next tag for that block, which it only does
+// after its whole previous call -- reads of this slot included -- finished
+// (stream order). Tags increase by one per call and compare modulo 2^32.
+//
+// Compared with a separate reduction kernel followed by an exchange kernel, the
+// fusion removes one launch and one kernel boundary from the end of every
+// sharded backward, and lets each block's exchange start as soon as its own
+// columns are summed.
 #include <cstdint>
 
 #include "sy_common.cuh"
@@ -29,8 +45,17 @@
 namespace sy {
 namespace {
 
-constexpr int kExThreads = 256;
+constexpr int kExThreads = 256;  // 8 warps: the partial-row sum of sy_dw_reduce
 constexpr int kExMaxWorld = 64;
+constexpr unsigned long long kExDefaultWaitNs = kWaitLimitNs;
+
+// The announcement: a system-scope release store per destination rank, after
+// the warp's slot stores (ordered by __syncwarp). 1: an explicit
+// __threadfence_system() before it as well; 2: fence.acq_rel.sys; 0: the
+// release store alone.
+#ifndef SY_TUNE_EXCHANGE_FENCE
+#define SY_TUNE_EXCHANGE_FENCE 1
+#endif
 
 __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -42,74 +67,108 @@ __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
   return v;
 }
 
-// Peer data is re-read every second call at the same address: never serve it
-// from a cache line filled by an earlier call.
+// Peer slots are re-read every second call at the same address: never serve
+// them from a cache line filled by an earlier call.
 __device__ __forceinline__ float ld_volatile_f(const float* p) {
   float v;
   asm volatile("ld.volatile.global.f32 %0, [%1];" : "=f"(v) : "l"(p) : "memory");
   return v;
 }
 
-__device__ __forceinline__ float4 ld_volatile_f4(const float* p) {
-  float4 v;
-  asm volatile("ld.volatile.global.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "l"(p)
-               : "memory");
-  return v;
-}
-
 __global__ void __launch_bounds__(kExThreads)
-    dw_exchange_kernel(const unsigned long long* __restrict__ bases, int world, int rank,
-                       long long slot_off, long long flag_off, unsigned tag, long long D,
-                       void* __restrict__ dw, int dw_dtype) {
-  __shared__ int ok;
-  if (threadIdx.x == 0) ok = 1;
-  // 1. announce (one thread per destination rank, first CTA only)
-  if (blockIdx.x == 0 && (int)threadIdx.x < world) {
-    __threadfence_system();
-    unsigned* f = reinterpret_cast<unsigned*>(bases[threadIdx.x] + flag_off) + rank;
-    st_release_sys(f, tag);
-  }
-  __syncthreads();
-  // 2. every CTA waits for all ranks' announcements of this tag
-  if ((int)threadIdx.x < world) {
-    const unsigned* f = reinterpret_cast<const unsigned*>(bases[rank] + flag_off) + threadIdx.x;
-    const unsigned long long t0 = globaltimer_ns();
-    for (uint32_t it = 0; (int)(ld_acquire_sys(f) - tag) < 0; ++it) {
-      if ((it & 63u) == 63u && globaltimer_ns() - t0 > kWaitLimitNs) {
+    reduce_exchange_kernel(const float* __restrict__ part, long long P, long long L,
+                           const unsigned long long* __restrict__ bases, int world, int rank,
+                           long long slot_off, long long flag_off, unsigned tag,
+                           void* __restrict__ out, int out_dtype, unsigned long long limit_ns,
+                           unsigned long long* __restrict__ timing,
+                           unsigned* __restrict__ fail_word) {
+  __shared__ float slice[8][33];
+  // Everything below reads the backward's partial rows.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const unsigned long long t_entry = globaltimer_ns();
+  const int lane = threadIdx.x & 31;
+  const int wp = threadIdx.x >> 5;
+  const long long nblk = (L + 31) / 32;
+  const unsigned long long own = bases[rank];
+  unsigned* const own_flags = reinterpret_cast<unsigned*>(own + flag_off);
+  float* const own_slot = reinterpret_cast<float*>(own + slot_off);
+
+  bool failed = false;  // warp 0: a wait of this CTA ran out; later blocks fail at once
+  for (long long blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    const long long col = blk * 32 + lane;
+    // 1. this rank's sum of its partial rows (sy_dw_reduce's order)
+    const float acc = col < L ? partial_rows_warp_sum(part, P, L, col, wp) : 0.f;
+    slice[wp][lane] = acc;
+    __syncthreads();
+    if (wp == 0) {
+      const unsigned long long t_reduced = lane == 0 ? globaltimer_ns() : 0ull;
+      float mine = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mine += slice[i][lane];
+      // 2. own slot, then the announcement to every rank
+      if (col < L) own_slot[col] = mine;
+      __syncwarp();
+      unsigned long long t_announced = 0;
+      for (int r = lane; r < world; r += 32) {
+#if SY_TUNE_EXCHANGE_FENCE == 1
+        __threadfence_system();
+#elif SY_TUNE_EXCHANGE_FENCE == 2
+        asm volatile("fence.acq_rel.sys;" ::: "memory");
+#endif
+        st_release_sys(reinterpret_cast<unsigned*>(bases[r] + flag_off) + (long long)rank * nblk + blk,
+                       tag);
+      }
+      if (lane == 0) t_announced = globaltimer_ns();
+      // 3. bounded wait for every rank's announcement of this block
+      bool ok = !failed;
+      for (int r = lane; ok && r < world; r += 32) {
+        const unsigned* f = own_flags + (long long)r * nblk + blk;
+        const unsigned long long t0 = globaltimer_ns();
+        for (uint32_t it = 0; (int)(ld_acquire_sys(f) - tag) < 0; ++it) {
+          if ((it & 63u) == 63u && globaltimer_ns() - t0 > limit_ns) {
+            ok = false;
+            break;
+          }
+        }
+      }
+      ok = __all_sync(0xffffffffu, ok);
+      failed = !ok;
+      const unsigned long long t_seen = lane == 0 ? globaltimer_ns() : 0ull;
+      // 4. rank-order sum (or the poison value after a timeout)
+      if (col < L) {
+        float total;
+        if (ok) {
+          total = rank == 0 ? mine : ld_volatile_f(reinterpret_cast<const float*>(bases[0] + slot_off) + col);
+          for (int r = 1; r < world; ++r)
+            total += r == rank ? mine
+                               : ld_volatile_f(reinterpret_cast<const float*>(bases[r] + slot_off) + col);
+        } else {
+          total = __int_as_float(0x7fc00000);  // quiet NaN: the gradient is unusable
+        }
+        store_any(out, out_dtype, col, total);
+      }
+      if (!ok && lane == 0) {
         record_device_error(kDevErrWaitTimeout);
-        ok = 0;
-        break;
+        if (fail_word) *reinterpret_cast<volatile unsigned*>(fail_word) = tag;
+      }
+      // timing[8] (block 0 of the call): calls; total and largest time from
+      // the announcement to the last peer's flag; total time from the
+      // kernel's start (after the backward completed) to the end of the
+      // block's sum; and the totals of its phases: the partial-row sum, the
+      // slot store and announcement, the peer reads and the output store
+      if (timing && lane == 0 && blk == 0) {
+        const unsigned long long t_end = globaltimer_ns();
+        const unsigned long long wait = t_seen - t_announced;
+        atomicAdd(timing + 0, 1ull);
+        atomicAdd(timing + 1, wait);
+        atomicMax(timing + 2, wait);
+        atomicAdd(timing + 3, t_end - t_entry);
+        atomicAdd(timing + 4, t_reduced - t_entry);
+        atomicAdd(timing + 5, t_announced - t_reduced);
+        atomicAdd(timing + 6, t_end - t_seen);
       }
     }
-  }
-  __syncthreads();
-  if (!ok) return;
-  // 3. rank-order sum, 4 columns per thread (slots are 16-byte aligned)
-  const long long stride = (long long)gridDim.x * blockDim.x * 4;
-  for (long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4; i < D; i += stride) {
-    if (i + 4 <= D) {
-      float4 acc = ld_volatile_f4(reinterpret_cast<const float*>(bases[0] + slot_off) + i);
-      for (int r = 1; r < world; ++r) {
-        const float4 x = ld_volatile_f4(reinterpret_cast<const float*>(bases[r] + slot_off) + i);
-        acc.x += x.x;
-        acc.y += x.y;
-        acc.z += x.z;
-        acc.w += x.w;
-      }
-      store_any(dw, dw_dtype, i, acc.x);
-      store_any(dw, dw_dtype, i + 1, acc.y);
-      store_any(dw, dw_dtype, i + 2, acc.z);
-      store_any(dw, dw_dtype, i + 3, acc.w);
-    } else {
-      for (long long k = i; k < D; ++k) {
-        float acc = ld_volatile_f(reinterpret_cast<const float*>(bases[0] + slot_off) + k);
-        for (int r = 1; r < world; ++r)
-          acc += ld_volatile_f(reinterpret_cast<const float*>(bases[r] + slot_off) + k);
-        store_any(dw, dw_dtype, k, acc);
-      }
-    }
+    __syncthreads();  // slice is reused by the next block of this CTA
   }
 }
 
@@ -118,22 +177,46 @@ int esize(int dtype) { return dtype == SY_F32 ? 4 : ((dtype == SY_BF16 || dtype 
 }  // namespace
 }  // namespace sy
 
-extern "C" int sy_dw_exchange(const void* peer_bases, int world, int rank, int64_t slot_off,
-                              int64_t flag_off, uint32_t tag, int64_t D, void* dw, int dw_dtype,
+extern "C" int64_t sy_dw_exchange_flags(int64_t L, int world) {
+  if (L < 0 || world < 1 || world > sy::kExMaxWorld) return -SY_ERR_ARG;
+  return (int64_t)world * ((L + 31) / 32);
+}
+
+extern "C" int sy_dw_exchange(const float* dw_partial, int64_t P, int64_t L, const void* peer_bases,
+                              int world, int rank, int64_t slot_off, int64_t flag_off, uint32_t tag,
+                              void* dw, int dw_dtype, uint64_t wait_limit_ns,
+                              unsigned long long* timing, unsigned int* fail_word,
                               sy_stream_t stream) {
   using namespace sy;
   if (!esize(dw_dtype)) return SY_ERR_DTYPE;
-  if (world < 1 || world > kExMaxWorld || rank < 0 || rank >= world || D < 0) return SY_ERR_ARG;
-  if (slot_off < 0 || flag_off < 0 || (slot_off % 16) != 0 || (flag_off % 4) != 0)
+  if (world < 1 || world > kExMaxWorld || rank < 0 || rank >= world || L < 0 || P < 1)
     return SY_ERR_ARG;
-  if (D == 0) return SY_OK;
-  if (!peer_bases || !dw) return SY_ERR_ARG;
-  const long long per_cta = (long long)kExThreads * 4;
-  long long grid = (D + per_cta - 1) / per_cta;
-  if (grid > 1024) grid = 1024;
-  dw_exchange_kernel<<<(unsigned)grid, kExThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const unsigned long long*>(peer_bases), world, rank, (long long)slot_off,
-      (long long)flag_off, tag, (long long)D, dw, dw_dtype);
-  const cudaError_t e = cudaGetLastError();
+  if (slot_off < 0 || flag_off < 0 || (slot_off % 4) != 0 || (flag_off % 4) != 0) return SY_ERR_ARG;
+  if (L == 0) return SY_OK;
+  if (!dw_partial || !peer_bases || !dw) return SY_ERR_ARG;
+  if (timing && (reinterpret_cast<uintptr_t>(timing) & 7u)) return SY_ERR_ARG;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return SY_ERR_CUDA;
+  const long long nblk = (L + 31) / 32;
+  long long grid = nblk < 2LL * sms ? nblk : 2LL * sms;  // resident at once (small CTAs)
+  if (grid < 1) grid = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(kExThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, reduce_exchange_kernel, dw_partial, (long long)P, (long long)L,
+                         static_cast<const unsigned long long*>(peer_bases), world, rank,
+                         (long long)slot_off, (long long)flag_off, (unsigned)tag, dw, dw_dtype,
+                         (unsigned long long)(wait_limit_ns ? wait_limit_ns : kExDefaultWaitNs),
+                         timing, fail_word);
+  if (e == cudaSuccess) e = cudaGetLastError();
   return e == cudaSuccess ? SY_OK : SY_ERR_CUDA;
 }

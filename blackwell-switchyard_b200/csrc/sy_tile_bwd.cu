@@ -321,21 +321,9 @@ __global__ void __launch_bounds__(256) dw_reduce_kernel(const float* __restrict_
   const int lane = threadIdx.x & 31;
   const int wp = threadIdx.x >> 5;
   const long long col = (long long)blockIdx.x * 32 + lane;
-  float acc = 0.f;
-  if (col < D) {
-    // all of a batch's loads are issued before the first add: one DRAM
-    // round trip per 32 rows instead of one per row
-    for (long long p0 = wp; p0 < P; p0 += 8 * 32) {
-      float x[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const long long p = p0 + 8 * i;
-        x[i] = p < P ? __ldcs(part + p * D + col) : 0.f;
-      }
-#pragma unroll
-      for (int i = 0; i < 32; ++i) acc += x[i];
-    }
-  }
+  // all of a batch's loads are issued before the first add: one DRAM round
+  // trip per 32 rows instead of one per row
+  const float acc = col < D ? partial_rows_warp_sum(part, P, D, col, wp) : 0.f;
   slice[wp][lane] = acc;
   __syncthreads();
   if (wp == 0 && col < D) {

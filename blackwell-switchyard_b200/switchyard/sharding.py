@@ -10,14 +10,15 @@ own fp32 partial and every rank adds all ranks' partials in rank order
 0..world-1, so all ranks hold the bitwise-same ``dw`` and the result is
 deterministic for a given partition.
 
-On CUDA ranks the partials cross NVLink as peer loads: each rank's dw
-reduction writes into a buffer every rank can address (torch symmetric memory,
-allocated once per group and D), and one kernel (``sy_dw_exchange``) announces,
-waits for all ranks with a bounded wait, and sums the peers' rows directly --
-no NCCL call on the step. Elsewhere (gloo on CPU, or if peer memory is not
-available, or with ``SWITCHYARD_DW_EXCHANGE=collective``) the rows are
-all-gathered with the process group and summed in the same order, which gives
-the same bits.
+On CUDA ranks the partials cross NVLink as peer loads: one kernel
+(``sy_dw_exchange``), launched as a programmatic dependent of the backward,
+sums the rank's partial rows into a buffer every rank can address (torch
+symmetric memory, allocated once per group and D), announces each 32-column
+block to every rank, waits for all ranks with a bounded wait, and adds the
+peers' rows directly -- no NCCL call and no second launch on the step.
+Elsewhere (gloo on CPU, or if peer memory is not available, or with
+``SWITCHYARD_DW_EXCHANGE=collective``) the rows are all-gathered with the
+process group and summed in the same order, which gives the same bits.
 """
 
 from __future__ import annotations
@@ -28,9 +29,10 @@ import torch
 import torch.distributed as dist
 
 from . import _native
-from .triton_op import DEFAULT_EPS, _backward, _forward, _validate
+from .triton_op import DEFAULT_EPS, _backward, _backward_partials, _forward, _validate
 
-__all__ = ["token_range", "exchange_dw", "block_attn_res_sharded", "block_attn_res_batched_sharded"]
+__all__ = ["token_range", "exchange_dw", "block_attn_res_sharded", "block_attn_res_batched_sharded",
+           "PeerExchange", "PeerExchangeError", "peer_exchange", "device_barrier"]
 
 
 def token_range(bt: int, world: int, rank: int) -> tuple[int, int]:
@@ -57,21 +59,50 @@ def exchange_dw(dw_local: torch.Tensor, group=None) -> torch.Tensor:
     return total
 
 
-class _PeerDw:
-    """The peer-memory dw exchange of one (process group, D, device): a buffer
-    every rank can address -- two fp32 slots of D floats, used alternately,
-    and one uint32 flag per rank -- and the device array of all ranks'
-    addresses of it. Built collectively on first use."""
+#: Bounded wait of the peer exchange, in nanoseconds. A legitimate wait lasts
+#: microseconds (the slowest rank's backward tail plus an NVLink round trip);
+#: after this long the kernel stops waiting, writes NaN into the gradient,
+#: records the device error word and stores the call's tag into the host-visible
+#: fail word that the next call checks. ``SWITCHYARD_EXCHANGE_WAIT_S`` overrides
+#: the default of 2 s.
+EXCHANGE_WAIT_LIMIT_NS = int(float(os.environ.get("SWITCHYARD_EXCHANGE_WAIT_S", "2")) * 1e9)
 
-    def __init__(self, group, d: int, device: torch.device):
+
+class PeerExchangeError(RuntimeError):
+    """A peer exchange's bounded wait ran out: a rank did not reach the step.
+    The gradient of that call is NaN; the exchange is unusable afterwards."""
+
+
+class PeerExchange:
+    """The peer-memory gradient exchange of one (process group, length L,
+    device): a buffer every rank can address -- two fp32 slots of L floats,
+    used alternately, and one uint32 flag per (rank, 32-column block) -- and the
+    device array of all ranks' addresses of it. Built collectively on first
+    use (:func:`peer_exchange`).
+
+    :meth:`reduce_exchange` is one launch (``sy_dw_exchange``): it sums this
+    rank's partial rows in ``sy_dw_reduce``'s order, publishes them, waits for
+    every rank (bounded) and adds all ranks' sums in rank order.
+
+    Failure handling: if a wait runs out, that call's output is NaN and its tag
+    lands in :attr:`fail` (pinned host memory the kernel writes, read by the
+    host without a synchronisation). Every call first checks it -- the host
+    queues work ahead of the GPU, so a timeout is seen by a later call, and at
+    the latest after the next synchronisation -- and then raises
+    :class:`PeerExchangeError`; the exchange stays broken, so no later call can
+    rewrite a slot a late peer may still read.
+    """
+
+    def __init__(self, group, length: int, device: torch.device):
         import torch.distributed._symmetric_memory as symm
 
         group = group if group is not None else dist.group.WORLD
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
-        self.d = d
-        self.slot_floats = (d + 3) // 4 * 4  # keeps the second slot 16-byte aligned
-        flag_floats = (self.world + 3) // 4 * 4
+        self.length = length
+        self.slot_floats = (length + 3) // 4 * 4  # keeps the second slot 16-byte aligned
+        nflags = _native.dw_exchange_flags(length, self.world)
+        flag_floats = (nflags + 3) // 4 * 4
         self.buf = symm.empty(2 * self.slot_floats + flag_floats, dtype=torch.float32,
                               device=device)
         self.buf.zero_()
@@ -81,45 +112,101 @@ class _PeerDw:
         self.bases = torch.tensor([p + delta for p in ptrs], dtype=torch.int64, device=device)
         self.flag_off = 2 * self.slot_floats * 4
         self.tag = 0
+        self.wait_limit_ns = EXCHANGE_WAIT_LIMIT_NS
+        self.fail = torch.zeros(1, dtype=torch.int32, pin_memory=True)
+        self.timing = None
+        self.broken = None
         torch.cuda.synchronize(device)
         dist.barrier(group)  # every rank's flags are zero before the first announcement
 
-    def next_slot(self):
-        """The slot this call's local dw goes into, and its byte offset."""
-        self.tag += 1
-        off = (self.tag & 1) * self.slot_floats
-        return self.buf[off: off + self.d], off * 4
+    def check(self) -> None:
+        """Raise if an earlier call of this exchange timed out (host read of the
+        fail word; no synchronisation)."""
+        if self.broken is None:
+            tag = int(self.fail[0])
+            if tag:
+                self.broken = (f"switchyard: peer gradient exchange (rank {self.rank} of "
+                               f"{self.world}) timed out waiting for a rank at call {tag}; that "
+                               "gradient is NaN and the exchange is no longer usable")
+        if self.broken is not None:
+            raise PeerExchangeError(self.broken)
 
-    def exchange(self, slot_off: int, dw: torch.Tensor) -> None:
-        _native.dw_exchange(self.bases, self.world, self.rank, slot_off, self.flag_off,
-                            self.tag, dw)
+    def reduce_exchange(self, part: torch.Tensor, out: torch.Tensor) -> None:
+        """``out`` [L] (any of the three dtypes) = sum over ranks, in rank
+        order, of each rank's fp32 sum of its partial rows ``part`` [P, L]."""
+        self.check()
+        self.tag += 1
+        slot_off = (self.tag & 1) * self.slot_floats * 4
+        _native.dw_exchange(part, self.bases, self.world, self.rank, slot_off, self.flag_off,
+                            self.tag, out, self.wait_limit_ns, self.timing, self.fail)
+
+    def start_timing(self) -> None:
+        """Count calls and phase nanoseconds from now on (device counters)."""
+        self.timing = torch.zeros(8, dtype=torch.int64, device=self.bases.device)
+
+    def read_timing(self) -> dict:
+        """Counters since :meth:`start_timing` (synchronises), per call of the
+        kernel's first block: mean and largest wait from this rank's
+        announcement to the last peer's flag; mean time from the kernel's start
+        to the end of its sum, and of its phases (partial-row sum, slot store
+        and announcement, peer reads and output store)."""
+        c = [int(x) for x in self.timing.tolist()]
+        k = max(c[0], 1)
+        return {"calls": c[0], "wait_mean_us": c[1] / k / 1e3, "wait_max_us": c[2] / 1e3,
+                "kernel_mean_us": c[3] / k / 1e3, "reduce_mean_us": c[4] / k / 1e3,
+                "announce_mean_us": c[5] / k / 1e3, "peer_sum_mean_us": c[6] / k / 1e3}
 
 
 _PEER: dict = {}
 _PEER_UNAVAILABLE: set = set()
 
 
-def _peer_dw(group, d: int, device: torch.device):
-    """The group's peer exchange for D, or None where the collective path is used."""
+def peer_exchange(group, length: int, device: torch.device):
+    """The group's peer exchange for ``length`` columns on ``device`` (built
+    collectively on first use), or None where the collective path is used: CPU
+    or single-rank groups, ``SWITCHYARD_DW_EXCHANGE=collective``, or no peer
+    memory on this system."""
     if device.type != "cuda" or os.environ.get("SWITCHYARD_DW_EXCHANGE") == "collective":
         return None
     world = dist.get_world_size(group)
     if world < 2:
         return None
     gname = (group or dist.group.WORLD).group_name
-    key = (gname, d, device.index)
+    key = (gname, length, device.index)
     if key in _PEER_UNAVAILABLE:
         return None
     peer = _PEER.get(key)
     if peer is None:
         try:
-            peer = _PEER[key] = _PeerDw(group, d, device)
+            peer = _PEER[key] = PeerExchange(group, length, device)
         except (RuntimeError, ImportError, AttributeError):
             # every rank takes the same branch: the allocation or the
             # rendezvous is unsupported on this system
             _PEER_UNAVAILABLE.add(key)
             return None
     return peer
+
+
+_BARRIER_LEN = 1  # the barrier's exchange is keyed by this length on its own group key
+
+
+def device_barrier(group=None, device: torch.device | None = None) -> None:
+    """Queue a barrier across the ranks' current CUDA streams: work queued after
+    it on any rank starts only once every rank's stream has reached it (one
+    single-value peer exchange; bounded wait). The host does not block. Used to
+    start ranks' timed regions together."""
+    device = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+    world = dist.get_world_size(group)
+    if world < 2:
+        return
+    gname = (group or dist.group.WORLD).group_name
+    key = ("barrier", gname, device.index)
+    peer = _PEER.get(key)
+    if peer is None:
+        peer = _PEER[key] = PeerExchange(group, _BARRIER_LEN, device)
+        peer.zero = torch.zeros(1, _BARRIER_LEN, dtype=torch.float32, device=device)
+        peer.sink = torch.empty(_BARRIER_LEN, dtype=torch.float32, device=device)
+    peer.reduce_exchange(peer.zero, peer.sink)
 
 
 class _ShardedBlockAttnRes(torch.autograd.Function):
@@ -136,12 +223,13 @@ class _ShardedBlockAttnRes(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad_out):
         v, w, stats = ctx.saved_tensors
-        peer = _peer_dw(ctx.group, w.shape[0], w.device)
+        peer = peer_exchange(ctx.group, w.shape[0], w.device)
         if peer is not None:
-            slot, off = peer.next_slot()
-            dv, _ = _backward(v, w, stats, grad_out, ctx.eps, torch.float32, dw_out=slot)
+            dv, part = _backward_partials(v, w, stats, grad_out, ctx.eps)
             dw = torch.empty_like(w)
-            peer.exchange(off, dw)
+            if part is not None:
+                with torch.cuda.device(v.device):
+                    peer.reduce_exchange(part, dw)
         else:
             dv, dw32 = _backward(v, w, stats, grad_out, ctx.eps, torch.float32)
             dw = exchange_dw(dw32, ctx.group).to(w.dtype)
@@ -195,11 +283,9 @@ class _ShardedBatched(torch.autograd.Function):
             p = _native.bwd_batched_partials(n, bt, d, s, v.dtype)
             part = torch.empty(p, s * d, device=v.device, dtype=torch.float32)
             _native.bwd_batched(v, q, g, dv, part, n, bt, d, s, ctx.eps)
-            peer = _peer_dw(ctx.group, s * d, q.device)
+            peer = peer_exchange(ctx.group, s * d, q.device)
             if peer is not None:
-                slot, off = peer.next_slot()
-                _native.dw_reduce(part, slot)
-                peer.exchange(off, dq.view(s * d))
+                peer.reduce_exchange(part, dq.view(s * d))
             else:
                 dq32 = torch.empty(s * d, device=v.device, dtype=torch.float32)
                 _native.dw_reduce(part, dq32)

@@ -1,10 +1,9 @@
 """Generate the golden fixtures by running the REFERENCE implementation.
 
-Run in a checkout where the reference (sabdulmajid/blackwell-switchyard) is
-available -- by default ``/root/reference`` (override with
-``SWITCHYARD_REFERENCE``) -- as::
+Run where a checkout of the reference (sabdulmajid/blackwell-switchyard) is
+available, naming its root by argument or by ``SWITCHYARD_REFERENCE``::
 
-    python tests/golden/make_golden.py
+    python tests/golden/make_golden.py <reference checkout>
 
 It imports the reference's own ``src/switchyard/reference.py`` and
 ``baselines.py`` (read-only), evaluates them in float64 on the deterministic
@@ -53,8 +52,18 @@ CASES = {
 }
 
 
+def reference_root() -> Path:
+    """The reference checkout: the first command-line argument, else
+    ``SWITCHYARD_REFERENCE``; there is no default location."""
+    where = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("SWITCHYARD_REFERENCE")
+    if not where:
+        raise SystemExit("name the reference checkout: make_golden.py <path> "
+                         "(or set SWITCHYARD_REFERENCE)")
+    return Path(where)
+
+
 def _load_reference():
-    root = Path(os.environ.get("SWITCHYARD_REFERENCE", "/root/reference")) / "src"
+    root = reference_root() / "src"
     sys.path.insert(0, str(root))
     spec = importlib.util.find_spec("switchyard.reference")
     if spec is None or not str(spec.origin).startswith(str(root)):

@@ -103,9 +103,10 @@ def _worker(rank, world, port, outdir):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_peer_dw_exchange_matches_collective_and_oracle(tmp_path):
-    world = 2
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_peer_dw_exchange_matches_collective_and_oracle(world, tmp_path):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = mp.get_context("spawn")
     port = _free_port()
     procs = [ctx.Process(target=_worker, args=(r, world, port, str(tmp_path))) for r in range(world)]
