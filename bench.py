@@ -85,6 +85,12 @@ def parse_args():
                          "T=2048 per GPU, DDP over NCCL under torchrun; one JSON line")
     ap.add_argument("--decoder-batch", type=int, default=4)
     ap.add_argument("--decoder-seq", type=int, default=2048)
+    ap.add_argument("--grid", action="store_true",
+                    help="no bench line: BASELINE config 4, the shape grid N x B x T x D in bf16 with "
+                         "the token axis sharded over the torchrun world; fwd and fwd+bwd per shape, "
+                         "checked against a float64 evaluation; one JSON line per shape")
+    ap.add_argument("--grid-max-shapes", type=int, default=0,
+                    help="with --grid: stop after this many shapes (0: all)")
     ap.add_argument("--sweep", action="store_true",
                     help="no bench line: time forward, backward and the fwd+bwd step through the "
                          "C ABI for bf16, fp16 and fp32 at a few shapes, one JSON line each")
@@ -360,6 +366,22 @@ def kernel_times(native, v, w, dout, steps, flush, stream):
     return res, p
 
 
+def launch_floor(dev, steps, flush):
+    """Device time, by the bench's own method (L2 flush, spin kernel, CUDA
+    events around one launch), of this library's smallest kernel: sy_dw_reduce
+    over one partial row of 32 columns (one CTA, 32 loads). What any single
+    kernel measures at least with this method: the two events plus launching
+    and retiring a grid."""
+    from switchyard import _native
+
+    part = torch.zeros(1, 32, device=dev, dtype=torch.float32)
+    out = torch.empty(32, device=dev, dtype=torch.float32)
+    fn = lambda: _native.dw_reduce(part, out)  # noqa: E731
+    for _ in range(3):
+        fn()
+    return summarize(timed_steps(fn, steps, flush))["mean_ms"] * 1e3
+
+
 def batched_times(v, steps, flush, hbm_gbs, qs=(1, 4, 8, 16)):
     """block_attn_res_batched at Q queries. Roofline: the larger of the HBM time
     (algorithmic bytes at the measured copy bandwidth) and the FP32 time
@@ -502,6 +524,44 @@ def stage_times(v, steps, flush, hbm_gbs):
             res[name] = {"us": st["mean_ms"] * 1e3, "bytes": byts,
                          "tbps": byts / (st["mean_ms"] * 1e-3) / 1e12,
                          "frac": byts / (hbm_gbs * 1e9) / (st["mean_ms"] * 1e-3)}
+    return res
+
+
+def host_cost(dev, calls=400):
+    """Host time per call of the public API on a tiny shape (N=9, 8 tokens,
+    D=2048 bf16; the kernels take a few microseconds, so the host is the
+    slower side and nothing waits on the GPU): the forward under no_grad, the
+    forward + backward through autograd, and one raw C-ABI call (sy_plan_kind)
+    for the ctypes cost alone. Microseconds per call."""
+    from switchyard import _native, block_attn_res_triton
+
+    gen = torch.Generator(device=dev).manual_seed(5)
+    v = torch.randn(9, 1, 8, 2048, device=dev, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(2048, device=dev, generator=gen) / 45.0).to(torch.bfloat16)
+    g = torch.randn(1, 8, 2048, device=dev, generator=gen).to(torch.bfloat16)
+
+    def fwd():
+        with torch.no_grad():
+            block_attn_res_triton(v, w)
+
+    def fwd_bwd():
+        vv = v.detach().requires_grad_(True)
+        ww = w.detach().requires_grad_(True)
+        block_attn_res_triton(vv, ww).backward(g)
+
+    def raw():
+        _native.lib.sy_plan_kind(0, 9, 8, 2048, 1, 0)
+
+    res = {}
+    for name, fn in (("forward", fwd), ("forward_backward", fwd_bwd), ("ctypes_call", raw)):
+        for _ in range(20):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(calls):
+            fn()
+        res[name + "_us"] = (time.perf_counter() - t0) / calls * 1e6
+        torch.cuda.synchronize()
     return res
 
 
@@ -731,6 +791,7 @@ def run_ours(args):
     result = None
     if rank == 0:
         kt, p_rows = kernel_times(_native, v, w, dout, args.steps, flush, None)
+        floor_us = launch_floor(dev, args.steps, flush)
         value = world * tot_b / (mean_step * 1e-3) / 1e12
         bwd_ach = bwd_b / (kt["bwd"]["mean_ms"] * 1e-3) / 1e9
         fwd_ach = fwd_b / (kt["fwd"]["mean_ms"] * 1e-3) / 1e9
@@ -792,6 +853,9 @@ def run_ours(args):
                 "frac_of_speed_of_light": fwd_ach / sol_ach,
             },
             "kernels_ms": {k: v_["mean_ms"] for k, v_ in kt.items()},
+            # one-CTA kernel of ours timed the same way: the fixed cost of the
+            # method (two events, one grid launched and retired)
+            "launch_floor_us": floor_us,
             "dw_partial_rows": p_rows,
             # per step: forward, backward, and the dw reduction -- fused with the
             # peer exchange on N > 1 (sy_dw_exchange); on N > 1 also the per-step
@@ -805,6 +869,7 @@ def run_ours(args):
         result["batched"] = batched_times(v, max(20, args.steps // 4), flush, peak)
         result["batched_train"] = batched_train_times(v, max(10, args.steps // 10), flush, peak)
         result["arena_stage"] = stage_times(v, max(20, args.steps // 4), flush, peak)
+        result["host_us_per_call"] = host_cost(dev)
         result["e2e"] = e2e
     if rank == 0 and world == 1:
         result["cpu_baseline"] = cpu_baseline(args.cpu_seconds)
@@ -961,6 +1026,169 @@ def run_sweep(args):
             print(json.dumps(line), flush=True)
             del v, dout, dv, out, part
             torch.cuda.empty_cache()
+
+
+GRID_N = (2, 3, 5, 9, 17, 33)
+GRID_B = (1, 4)
+GRID_T = (4096, 16384, 65536)
+GRID_D = (1024, 2048, 4096, 8192)
+
+
+def f64_tokens(v, w, g, eps=1e-6):
+    """Float64 evaluation of the operator on a few tokens, on the GPU (the
+    sweep's checker; the math of reference.py:42-59 and its gradient):
+    v [N, K, D], w [D], g [K, D] -> out [K, D], dv [N, K, D], and the tokens'
+    contribution to dw [D]."""
+    v, w, g = v.double(), w.double(), g.double()
+    d = v.shape[-1]
+    r = torch.rsqrt(v.pow(2).mean(-1) + eps)              # [N, K]
+    a = torch.einsum("d,nkd->nk", w, v)
+    alpha = torch.softmax(a * r, dim=0)
+    out = torch.einsum("nk,nkd->kd", alpha, v)
+    G = torch.einsum("kd,nkd->nk", g, v)
+    dlogit = alpha * (G - (alpha * G).sum(0, keepdim=True))
+    da = dlogit * r
+    dssq = -dlogit * a * r.pow(3) / (2.0 * d)
+    dv = alpha[..., None] * g[None] + da[..., None] * w + 2.0 * dssq[..., None] * v
+    dw = torch.einsum("nk,nkd->d", da, v)
+    return out, dv, dw
+
+
+def f64_dw(v, w, g, eps=1e-6):
+    """The tokens' float64 contribution to dw (as f64_tokens, without dv)."""
+    v, w, g = v.double(), w.double(), g.double()
+    r = torch.rsqrt(v.pow(2).mean(-1) + eps)
+    a = torch.einsum("d,nkd->nk", w, v)
+    alpha = torch.softmax(a * r, dim=0)
+    G = torch.einsum("kd,nkd->nk", g, v)
+    da = alpha * (G - (alpha * G).sum(0, keepdim=True)) * r
+    return torch.einsum("nk,nkd->d", da, v)
+
+
+def rel_l2_t(got, want) -> float:
+    return ((got.double() - want).norm() / want.norm().clamp_min(1e-300)).item()
+
+
+def bf16_floor(want) -> float:
+    """Relative L2 error of rounding the float64 values to bf16 (the dtype
+    floor the parity bar is a multiple of)."""
+    return rel_l2_t(want.to(torch.bfloat16), want)
+
+
+def run_grid(args):
+    """N in GRID_N, B in GRID_B, T in GRID_T, D in GRID_D,
+    bf16, v ~ N(0,1), w ~ N(0, 1/D), dout ~ N(0,1), each rank generating its
+    own contiguous token shard (seed 1000 + rank; w shared). Shapes whose
+    per-GPU footprint (v, dv, dout, out, statistics, partial rows) does not fit
+    in 85 % of the free memory are skipped, as the reference skips its > 24
+    GiB cases (bench/bench_operator.py:321-324).
+
+    Per shape: the forward and the fwd+bwd step (forward, backward, dw
+    reduction fused with the peer exchange on N > 1), each timed with CUDA
+    events after a device barrier across the ranks (max over ranks of the
+    mean), L2 flushed before each; TB/s of the global algorithmic bytes and the
+    per-GPU fraction of the measured copy peak. Checked in float64 on the GPU:
+    out and dv on 8 sampled tokens per rank, dw over every token (chunked) --
+    relative L2 against the float64 values as a multiple of the bf16 floor."""
+    import torch.distributed as dist
+
+    from switchyard import block_attn_res_triton, sharding
+    from switchyard.sharding import block_attn_res_sharded, token_range
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+    align = (lambda: sharding.device_barrier(None, dev)) if world > 1 else None
+    op = block_attn_res_sharded if world > 1 else block_attn_res_triton
+    peak = load_peak_field("hbm_gbs") or FALLBACK_HBM_GBS
+    flush = L2Flush(dev)
+    shapes = sorted(((n, b, t, d) for n in GRID_N for b in GRID_B for t in GRID_T for d in GRID_D),
+                    key=lambda s: (s[0] * s[1] * s[2] * s[3], s))
+    done = 0
+    for n, b, t, d in shapes:
+        if args.grid_max_shapes and done >= args.grid_max_shapes:
+            break
+        bt = b * t
+        lo, hi = token_range(bt, world, rank)
+        btl = hi - lo
+        free, _ = torch.cuda.mem_get_info(dev)
+        need = ((2 * n + 2) * btl * d * 2 + btl * 128 * 4 + 1024 * d * 4) * 1.05
+        fits = torch.tensor([1.0 if need < 0.85 * free else 0.0], device=dev)
+        if world > 1:
+            dist.all_reduce(fits, op=dist.ReduceOp.MIN)
+        line = {"shape": {"N": n, "B": b, "T": t, "D": d}, "world": world, "dtype": "bf16",
+                "tokens_per_rank": btl}
+        if fits.item() < 1.0:
+            if rank == 0:
+                line["skipped"] = f"per-GPU footprint {need / 2**30:.1f} GiB > 85% of free memory"
+                print(json.dumps(line), flush=True)
+            continue
+        gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+        v = torch.empty(n, 1, btl, d, device=dev, dtype=torch.bfloat16).normal_(generator=gen)
+        dout = torch.empty(1, btl, d, device=dev, dtype=torch.bfloat16).normal_(generator=gen)
+        gw = torch.Generator(device=dev).manual_seed(1)
+        w = (torch.randn(d, device=dev, generator=gw) / math.sqrt(d)).to(torch.bfloat16)
+        fwd_b, _, tot_b = alg_bytes(n, 1, btl, d)
+        est_ms = tot_b / 5e9
+        steps = int(min(20, max(3, 300 / max(est_ms, 1e-3))))
+        res = {}
+
+        def fwd():
+            with torch.no_grad():
+                op(v, w)
+
+        def step():
+            vv = v.detach().requires_grad_(True)
+            ww = w.detach().requires_grad_(True)
+            op(vv, ww).backward(dout)
+
+        for name, fn, byts in (("fwd", fwd, fwd_b), ("fwd_bwd", step, tot_b)):
+            for _ in range(2):
+                fn()
+                if align is not None:
+                    align()
+            ms = statistics.fmean(timed_steps(fn, steps, flush, align=align))
+            if world > 1:
+                tt = torch.tensor([ms], device=dev, dtype=torch.float64)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                ms = tt.item()
+            res[name] = {"us": ms * 1e3, "tbps": world * byts / (ms * 1e-3) / 1e12,
+                         "frac_of_peak": byts / (ms * 1e-3) / 1e9 / peak}
+        # parity: out and dv on 8 sampled tokens of this rank, dw over all tokens
+        vv = v.detach().requires_grad_(True)
+        ww = w.detach().requires_grad_(True)
+        out = op(vv, ww)
+        out.backward(dout)
+        pick = torch.linspace(0, btl - 1, 8, device=dev).long()
+        o64, dv64, _ = f64_tokens(v[:, 0, pick], w, dout[0, pick])
+        err = torch.tensor([rel_l2_t(out[0, pick], o64) / bf16_floor(o64),
+                            rel_l2_t(vv.grad[:, 0, pick], dv64) / bf16_floor(dv64)],
+                           device=dev, dtype=torch.float64)
+        dw64 = torch.zeros(d, device=dev, dtype=torch.float64)
+        chunk = max(1, int(2**26 // (n * d)))  # 512 MiB per float64 temporary
+        for c0 in range(0, btl, chunk):
+            dw64 += f64_dw(v[:, 0, c0:c0 + chunk], w, dout[0, c0:c0 + chunk])
+        if world > 1:
+            dist.all_reduce(err, op=dist.ReduceOp.MAX)
+            dist.all_reduce(dw64)
+        dw_err = rel_l2_t(ww.grad, dw64) / bf16_floor(dw64)
+        res["parity_x_bf16_floor"] = {"out_sampled": err[0].item(), "dv_sampled": err[1].item(),
+                                      "dw": dw_err}
+        line.update(res)
+        line["timed_steps"] = steps
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        del v, dout, vv, ww, out, dw64
+        torch.cuda.empty_cache()
+        done += 1
+    if world > 1:
+        dist.barrier()
+        sharding._PEER.clear()
+        dist.destroy_process_group()
 
 
 def run_decoder(args):
@@ -1155,6 +1383,9 @@ def main():
         return
     if args.decoder:
         run_decoder(args)
+        return
+    if args.grid:
+        run_grid(args)
         return
     if args.impl == "reference":
         run_reference(args)

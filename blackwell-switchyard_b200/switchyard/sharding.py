@@ -300,4 +300,8 @@ def block_attn_res_batched_sharded(v_local: torch.Tensor, queries: torch.Tensor,
     sharded like :func:`block_attn_res_sharded`): output and ``dv`` stay local,
     ``queries.grad`` is the full-batch gradient, bitwise the same on every rank.
     Every rank must call it, in the same order, with the same ``queries``."""
+    from .two_phase import _check_batched, _check_trainable
+
+    _check_batched(v_local, queries)
+    _check_trainable(v_local, queries)
     return _ShardedBatched.apply(v_local, queries, eps, group)

@@ -58,6 +58,20 @@ def _check_batched(v: torch.Tensor, queries: torch.Tensor) -> None:
     _native.dtype_code(v.dtype)
 
 
+#: Queries the batched backward takes (``sy_bwd_batched``); the forward takes any number.
+BATCHED_TRAIN_MAX_QUERIES = 16
+
+
+def _check_trainable(v: torch.Tensor, queries: torch.Tensor) -> None:
+    """Refuse, before the forward runs, a batched call whose backward could not
+    run: more than BATCHED_TRAIN_MAX_QUERIES queries while a gradient is wanted."""
+    wants_grad = torch.is_grad_enabled() and (v.requires_grad or queries.requires_grad)
+    if wants_grad and queries.shape[0] > BATCHED_TRAIN_MAX_QUERIES:
+        raise ValueError(
+            f"the batched backward takes at most {BATCHED_TRAIN_MAX_QUERIES} queries, got "
+            f"{queries.shape[0]}; split the queries, or run the forward under torch.no_grad()")
+
+
 def _forward_stats(v: torch.Tensor, queries: torch.Tensor, eps: float, raw: bool):
     """One launch: out ``[S, B, T, D]`` (normalised, or unnormalised when
     ``raw``) and the fp32 statistics ``[S, B*T, 2]`` = (max logit, sum of
@@ -200,7 +214,8 @@ def block_attn_res_batched_train(
 ) -> torch.Tensor:
     """``block_attn_res_batched`` with a backward: output ``[S, B, T, D]``,
     entry ``s`` equal to ``block_attn_res_triton(v, queries[s], eps)``, and
-    gradients for ``v`` and ``queries`` (``S <= 16``). Same validation and
+    gradients for ``v`` and ``queries`` (``S <= 16``: more queries with a
+    gradient wanted are refused before the forward). Same validation and
     messages as the reference's batched API (``triton_op.py:463-474``)."""
     if queries.ndim == 2 and queries.shape[0] == 1:
         # one query: the single-query operator's kernels (the same forward
@@ -208,4 +223,6 @@ def block_attn_res_batched_train(
         # saved statistics), queries' gradient through the index
         _check_batched(v, queries)
         return _BlockAttnResTritonFn.apply(v, queries[0], eps).unsqueeze(0)
+    _check_batched(v, queries)
+    _check_trainable(v, queries)
     return _BlockAttnResBatched.apply(v, queries, eps)

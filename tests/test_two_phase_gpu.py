@@ -187,3 +187,23 @@ def test_two_phase_api_errors():
     o, m, ell = attn_with_stats(v, q)
     with pytest.raises(ValueError, match="same shape"):
         merge_online_softmax(o, m, ell, o[:1], m[:1], ell[:1])
+
+
+def test_more_than_16_queries_refused_before_the_forward_when_training():
+    """The batched backward takes at most 16 queries: with a gradient wanted, a
+    larger S is refused before anything runs (single-GPU and sharded ops);
+    without one the forward runs for any S."""
+    from switchyard.sharding import block_attn_res_batched_sharded
+
+    v, q, _ = make((3, 1, 8, 64), 17, torch.bfloat16, seed=3)
+    with pytest.raises(ValueError, match="at most 16 queries"):
+        block_attn_res_batched_train(v.clone().requires_grad_(True), q)
+    with pytest.raises(ValueError, match="at most 16 queries"):
+        block_attn_res_batched_train(v, q.clone().requires_grad_(True))
+    with pytest.raises(ValueError, match="at most 16 queries"):
+        block_attn_res_batched_sharded(v.clone().requires_grad_(True), q)
+    with torch.no_grad():
+        out = block_attn_res_batched_train(v.clone().requires_grad_(True), q)
+    assert out.shape == (17, 1, 8, 64)
+    out = block_attn_res_batched_train(v, q)  # nothing requires a gradient
+    assert out.shape == (17, 1, 8, 64) and not out.requires_grad
