@@ -726,9 +726,12 @@ def run_ours(args):
     mean_step, mean_fwd = st_step["mean_ms"], st_fwd["mean_ms"]
     per_rank = None
     if world > 1:
-        # the same step timed without the per-step device barrier (the ranks
-        # then start each step after their own flush, so each rank's events
-        # also hold the other ranks' skew): reported beside the aligned number
+        # the same step timed without the per-step device barrier, started
+        # right after a host barrier as an unaligned loop would be: each
+        # rank's events then also hold the other ranks' skew (host jitter at
+        # the start, flush differences); reported beside the aligned number
+        torch.cuda.synchronize()
+        dist.barrier()
         unaligned = summarize(timed_steps(step, args.steps, flush))
         # the exchange kernel alone, with the backward's own partial rows
         from switchyard.triton_op import _backward_partials, _forward

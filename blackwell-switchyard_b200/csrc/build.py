@@ -7,9 +7,12 @@ Python package that loads it. The library links the *shared* CUDA runtime, so
 in a process that already imported torch it uses torch's runtime and sees the
 same current device.
 
+Then the thin PyTorch C++ extension over that C ABI (``torch_ext/``) is
+compiled with g++ against torch's headers into ``switchyard/_sy_torch.so``.
+
 Usage: ``python build.py [--force] [--jobs N]``. Rebuilds only when the
 content of a source, header or of this script changed since the last build (a
-hash stamp beside the library; file times are unreliable after copies).
+hash stamp beside each library; file times are unreliable after copies).
 """
 
 from __future__ import annotations
@@ -114,6 +117,66 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False,
     return lib
 
 
+# ---------------------------------------------------------------------------
+# the PyTorch C++ extension over the C ABI (switchyard/_sy_torch*.so)
+# ---------------------------------------------------------------------------
+
+EXT_SRC = HERE / "torch_ext" / "sy_torch.cpp"
+EXT = PKG / "_sy_torch.so"
+EXT_STAMP = PKG / "_sy_torch.stamp"
+
+
+def _ext_cmd() -> list[str]:
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension
+
+    inc = [f"-I{p}" for p in cpp_extension.include_paths()]
+    inc += [f"-I{sysconfig.get_paths()['include']}", f"-I{INCLUDE}"]
+    cuda_home = cpp_extension.CUDA_HOME or "/usr/local/cuda"
+    inc.append(f"-I{Path(cuda_home) / 'include'}")
+    libs = [f"-L{p}" for p in cpp_extension.library_paths()]
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    return ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden",
+            f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_API_INCLUDE_EXTENSION_H",
+            "-DTORCH_EXTENSION_NAME=_sy_torch", *inc, str(EXT_SRC), *libs,
+            "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu", "-ltorch_cuda", "-ltorch_python",
+            f"-L{PKG}", "-l:libswitchyard_b200.so", "-Wl,-rpath,$ORIGIN"]
+
+
+def _ext_digest() -> str:
+    import torch
+
+    h = hashlib.sha256()
+    for p in [EXT_SRC, *sorted(INCLUDE.glob("*.h")), Path(__file__)]:
+        h.update(p.name.encode())
+        h.update(p.read_bytes())
+    h.update(torch.__version__.encode())
+    return h.hexdigest()
+
+
+def ext_up_to_date() -> bool:
+    return EXT.exists() and EXT_STAMP.exists() and EXT_STAMP.read_text().strip() == _ext_digest()
+
+
+def build_ext(force: bool = False) -> Path:
+    """Compile the extension (g++ against torch's headers, linked to the C-ABI
+    library beside it). Rebuilds only when its source, the header or torch
+    changed."""
+    if not force and ext_up_to_date():
+        return EXT
+    tmp = EXT.with_suffix(".so.tmp")
+    cmd = _ext_cmd()
+    cmd[cmd.index(str(EXT_SRC)) + 1:cmd.index(str(EXT_SRC)) + 1] = ["-o", str(tmp)]
+    _, rc, log = _run(cmd)
+    if rc != 0:
+        raise RuntimeError(f"extension build failed ({rc}): {' '.join(cmd)}\n{log}")
+    os.replace(tmp, EXT)
+    EXT_STAMP.write_text(_ext_digest() + "\n")
+    return EXT
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--force", action="store_true")
@@ -121,6 +184,7 @@ def main() -> int:
     ap.add_argument("-v", "--verbose", action="store_true")
     a = ap.parse_args()
     print(build(force=a.force, jobs=a.jobs, verbose=a.verbose))
+    print(build_ext(force=a.force))
     return 0
 
 

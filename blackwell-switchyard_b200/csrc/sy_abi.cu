@@ -313,9 +313,10 @@ struct StreamBwdPlan {
   int64_t smem = 0;
 };
 
-// Row-stream backward: rows of exactly 128 * K chunks, K = 2 .. 16 warps per
-// token (4 .. 32 KiB rows at 2 bytes per element), N <= 32. Whole tokens per
-// token stream, as evenly as possible (as the forward's re-read stream).
+// Row-stream backward: rows of exactly 128 * K chunks, K = 1 .. 16 warps per
+// token (2 .. 32 KiB rows at 2 bytes per element), N <= 64. Whole tokens per
+// token stream, as evenly as possible (as the forward's re-read stream). It
+// runs where the register tile does not (N > 16, or rows over 4 KiB).
 StreamBwdPlan plan_stream_bwd(int64_t N, int64_t BT, int64_t D, int dtype, const DevInfo& di) {
   StreamBwdPlan p;
   const int es = esize_of(dtype);
@@ -327,7 +328,7 @@ StreamBwdPlan plan_stream_bwd(int64_t N, int64_t BT, int64_t D, int dtype, const
   const int64_t per_warp = 32 * kStreamBwdCpl;
   if (rc % per_warp) return p;
   const int64_t kw = rc / per_warp;
-  if (kw < 2 || kw > 16) return p;
+  if (kw < 1 || kw > 16) return p;
   const int64_t max_streams = kStreamBwdThreads / 32 / kw;
   const int64_t g0 = BT < di.sms ? BT : di.sms;
   const int64_t t = (BT + g0 - 1) / g0;                // tokens per CTA
@@ -648,7 +649,7 @@ int sy_bwd(const void* v, const void* w, const void* g, const float* stats, void
   cudaError_t e = dev_info(&di);
   if (e != cudaSuccess) return cuda_status(e, "sy_bwd: device query");
   // Order: the register tile (N <= 16, rows up to 4 KiB), the row stream
-  // (rows of 128 * K chunks, N <= 32), the shared-memory tile, generic.
+  // (rows of 128 * K chunks, N <= 64), the shared-memory tile, generic.
   TilePlan p = plan_tile(kOpBwd, N, BT, D, dtype, di);
   p.c.eps = eps;
   const bool aligned = al16(v) && al16(g) && al16(stats) && al16(dv) && al16(dw_partial);

@@ -9,9 +9,14 @@ static cudaError_t launch_stream_bwd_t(const StreamBwdCfg& c, int grid, const vo
                                        const float* stats, void* dv, float* dw_partial,
                                        cudaStream_t st) {
   if (c.warps * 32 > kStreamBwdThreads) return cudaErrorInvalidConfiguration;
-  return launch_smem_pdl(stream_bwd_kernel<T>, grid, dim3(c.warps * 32),
-                     stream_bwd_smem_layout(c).total, st, static_cast<const T*>(v), w, w_dtype,
-                     static_cast<const T*>(g), stats, static_cast<T*>(dv), dw_partial, c);
+  if (c.N > 32)
+    return launch_smem_pdl(stream_bwd_kernel<T, 2>, grid, dim3(c.warps * 32),
+                           stream_bwd_smem_layout(c).total, st, static_cast<const T*>(v), w,
+                           w_dtype, static_cast<const T*>(g), stats, static_cast<T*>(dv),
+                           dw_partial, c);
+  return launch_smem_pdl(stream_bwd_kernel<T, 1>, grid, dim3(c.warps * 32),
+                         stream_bwd_smem_layout(c).total, st, static_cast<const T*>(v), w, w_dtype,
+                         static_cast<const T*>(g), stats, static_cast<T*>(dv), dw_partial, c);
 }
 
 cudaError_t launch_stream_bwd(const StreamBwdCfg& c, int grid, int dtype, const void* v,

@@ -2,7 +2,8 @@
 //
 // The register-tile backward holds a token's N source rows in registers; at
 // 16 KiB rows (D = 8192 bf16) or N > 16 they no longer fit. Here K warps share
-// each token, warp k owning chunks 128k .. 128k+127 of every row (4 per lane),
+// each token (K = 1 .. 16: rows of 2 to 32 KiB at two bytes per element), warp
+// k owning chunks 128k .. 128k+127 of every row (4 per lane),
 // and the token's rows stream through the K warps' shared ring of R row
 // buffers (cp.async.bulk, one mbarrier per buffer) in the order
 //
@@ -17,7 +18,8 @@
 //   S = sum_n alpha_n G_n,  dlogit_n = alpha_n (G_n - S),
 //   da_n = dlogit_n r_n,    cv_n = -dlogit_n logit_n r_n^2 / D,
 //
-// held by lane n. Pass B reads each row a second time -- the copy that pass A
+// held by lane n mod 32 (in its register slot n / 32: N <= 64, one slot per
+// 32 sources). Pass B reads each row a second time -- the copy that pass A
 // loaded with an evict-last hint, normally still in L2 -- and writes
 //
 //   dv_n = alpha_n g + da_n w + cv_n v_n,     dw += da_n v_n  (registers).
@@ -53,8 +55,9 @@ struct StreamBwdSmem {
 };
 
 // fp32 w (as planes of float4, like the forward), the streams' rings and full
-// barriers, the per-token exchange of G parts ([streams][2][kw][32] floats,
-// double-buffered by token parity) and the buffer-release counters.
+// barriers, the per-token exchange of G parts ([streams][2][kw][64] floats,
+// double-buffered by token parity; 32 per register slot) and the
+// buffer-release counters.
 __host__ __device__ inline StreamBwdSmem stream_bwd_smem_layout(const StreamBwdCfg& c) {
   const int kw = c.kw > 0 ? c.kw : 1;
   const size_t streams = (size_t)(c.warps / kw);
@@ -63,7 +66,7 @@ __host__ __device__ inline StreamBwdSmem stream_bwd_smem_layout(const StreamBwdC
   s.ring_off = ((size_t)c.D * 4 + 127) / 128 * 128;
   s.bar_off = s.ring_off + streams * c.ring * c.row_bytes;
   s.xg_off = s.bar_off + streams * c.ring * 8;
-  s.cnt_off = s.xg_off + streams * 2 * kw * 32 * 4;
+  s.cnt_off = s.xg_off + streams * 2 * kw * 64 * 4;
   s.total = s.cnt_off + (streams * c.ring * 4 + 15) / 16 * 16;
   return s;
 }
@@ -75,14 +78,15 @@ __host__ __device__ inline StreamBwdSmem stream_bwd_smem_layout(const StreamBwdC
 #endif
 constexpr int kStreamBwdThreads = 32 * SY_TUNE_STREAM_BWD_WARPS;
 constexpr int kStreamBwdCpl = 4;   // 16-byte chunks per lane and row
-constexpr int kStreamBwdMaxN = 32;  // lane n holds source n's coefficients
+constexpr int kStreamBwdMaxN = 64;  // lane n % 32, register slot n / 32, holds source n
 
 // L2 hint for pass A's copy of a row (pass B reads it again).
 #ifndef SY_TUNE_STREAM_BWD_KEEP
 #define SY_TUNE_STREAM_BWD_KEEP 1  // 1: evict_last, 0: evict_first
 #endif
 
-template <typename T>
+// SL: register slots of per-source coefficients per lane (1: N <= 32, 2: N <= 64).
+template <typename T, int SL>
 __global__ void __launch_bounds__(kStreamBwdThreads, 1)
     stream_bwd_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
                       const T* __restrict__ gin, const float* __restrict__ stats,
@@ -103,9 +107,9 @@ __global__ void __launch_bounds__(kStreamBwdThreads, 1)
   const int K = c.kw;
   const int RC = c.row_chunks;
   const int RB = c.row_bytes;
-  if (K < 2 || K > 16 || c.warps % K != 0 || c.warps != (int)(blockDim.x >> 5) || c.ring < 2 ||
-      RC != 32 * CPL * K || RB != 16 * RC || c.N < 1 || c.N > kStreamBwdMaxN ||
-      c.warps / K > 15) {
+  if (K < 1 || K > 16 || c.warps % K != 0 || c.warps != (int)(blockDim.x >> 5) || c.ring < 2 ||
+      RC != 32 * CPL * K || RB != 16 * RC || c.N < 1 || c.N > 32 * SL ||
+      (K > 1 && c.warps / K > 15)) {
     if (tid == 0) record_device_error(kDevErrBadPlan);
     return;
   }
@@ -131,7 +135,7 @@ __global__ void __launch_bounds__(kStreamBwdThreads, 1)
   const int nrows = ntok * LT;   // the planner keeps this below 2^31
   unsigned char* ring = ring0 + (size_t)gi * c.ring * RB;
   uint64_t* bar = bars + gi * c.ring;
-  float* xg = xg0 + (size_t)gi * 2 * K * 32;
+  float* xg = xg0 + (size_t)gi * 2 * K * 64;
   int* cnt = cnt0 + gi * c.ring;
   const size_t nstride = (size_t)c.BT * RB;
   const unsigned char* vb = reinterpret_cast<const unsigned char*>(v);
@@ -187,10 +191,16 @@ __global__ void __launch_bounds__(kStreamBwdThreads, 1)
   uint32_t ring_ph = 0;
   for (int j = 0; j < ntok && ok; ++j) {
     const long long tok = tok0 + tstride * j;
-    // lane n < N: source n's saved logit and inverse RMS (used after pass A)
+    // lane n % 32, slot n / 32: source n's saved logit and inverse RMS
+    // (used after pass A)
     const float* st = stats + tok * c.stats_stride;
-    const float s_logit = lane < N ? st[lane] : 0.f;
-    const float s_r = lane < N ? st[N + lane] : 0.f;
+    float s_logit[SL], s_r[SL];
+#pragma unroll
+    for (int sl = 0; sl < SL; ++sl) {
+      const int n = lane + 32 * sl;
+      s_logit[sl] = n < N ? st[n] : 0.f;
+      s_r[sl] = n < N ? st[N + n] : 0.f;
+    }
     const float lse = st[2 * N + 1];
 
     // ---- g: to registers as fp32 ----
@@ -213,8 +223,10 @@ __global__ void __launch_bounds__(kStreamBwdThreads, 1)
       ++q;
     }
 
-    // ---- pass A: this warp's part of G_n = g . v_n, lane n keeps it ----
-    float myg = 0.f;
+    // ---- pass A: this warp's part of G_n = g . v_n, lane n % 32 keeps it ----
+    float myg[SL];
+#pragma unroll
+    for (int sl = 0; sl < SL; ++sl) myg[sl] = 0.f;
     for (int n = 0; n < N; ++n, ++q) {
       const int slot = ring_slot;
       const uint32_t ph = ring_ph;
@@ -240,30 +252,54 @@ __global__ void __launch_bounds__(kStreamBwdThreads, 1)
       float s = acc[0].x + acc[0].y;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(kFull, s, off);
-      if (lane == n) myg = s;
+#pragma unroll
+      for (int sl = 0; sl < SL; ++sl)
+        if (n >> 5 == sl && lane == (n & 31)) myg[sl] = s;  // (the slot test is warp-uniform)
     }
     if (!ok) break;
 
     // ---- the K warps' parts of G, added in warp order by every warp ----
-    float* xr = xg + (j & 1) * K * 32;
-    xr[wk * 32 + lane] = myg;
-    named_sync(1 + gi, 32 * K);
-    float G = xr[lane];
-    for (int k2 = 1; k2 < K; ++k2) G += xr[k2 * 32 + lane];
+    float* xr = xg + (j & 1) * K * 64;
+#pragma unroll
+    for (int sl = 0; sl < SL; ++sl) xr[wk * 64 + 32 * sl + lane] = myg[sl];
+    if (K > 1)
+      named_sync(1 + gi, 32 * K);
+    else
+      __syncwarp();
+    float G[SL];
+#pragma unroll
+    for (int sl = 0; sl < SL; ++sl) {
+      G[sl] = xr[32 * sl + lane];
+      for (int k2 = 1; k2 < K; ++k2) G[sl] += xr[k2 * 64 + 32 * sl + lane];
+    }
 
-    // ---- coefficients: lane n < N owns source n ----
-    const float alpha = lane < N ? expf(s_logit - lse) : 0.f;
-    const float S = warp_sum(alpha * G);
-    const float dl = alpha * (G - S);
-    const float da_l = dl * s_r;
-    const float cv_l = -dl * s_logit * s_r * s_r * inv_d;
+    // ---- coefficients: lane n % 32, slot n / 32, owns source n ----
+    float alpha[SL], da_l[SL], cv_l[SL];
+    float ag = 0.f;
+#pragma unroll
+    for (int sl = 0; sl < SL; ++sl) {
+      alpha[sl] = lane + 32 * sl < N ? expf(s_logit[sl] - lse) : 0.f;
+      ag = sl == 0 ? alpha[0] * G[0] : fmaf(alpha[sl], G[sl], ag);
+    }
+    const float S = warp_sum(ag);
+#pragma unroll
+    for (int sl = 0; sl < SL; ++sl) {
+      const float dl = alpha[sl] * (G[sl] - S);
+      da_l[sl] = dl * s_r[sl];
+      cv_l[sl] = -dl * s_logit[sl] * s_r[sl] * s_r[sl] * inv_d;
+    }
 
     // ---- pass B: dv_n = alpha_n g + da_n w + cv_n v_n ; dw += da_n v_n ----
     T* dtok = dv + (size_t)tok * c.D + (size_t)cb * VEC;
     for (int n = 0; n < N; ++n, ++q) {
-      const float ka = __shfl_sync(kFull, alpha, n);
-      const float kd = __shfl_sync(kFull, da_l, n);
-      const float kc = __shfl_sync(kFull, cv_l, n);
+      // source n's coefficients from lane n % 32, slot n / 32 (warp-uniform)
+      float a_src = alpha[0], d_src = da_l[0], c_src = cv_l[0];
+#pragma unroll
+      for (int sl = 1; sl < SL; ++sl)
+        if (n >> 5 == sl) a_src = alpha[sl], d_src = da_l[sl], c_src = cv_l[sl];
+      const float ka = __shfl_sync(kFull, a_src, n & 31);
+      const float kd = __shfl_sync(kFull, d_src, n & 31);
+      const float kc = __shfl_sync(kFull, c_src, n & 31);
       const int slot = ring_slot;
       const uint32_t ph = ring_ph;
       if (++ring_slot == c.ring) {

@@ -20,6 +20,12 @@ logit and the log-sum-exp). The backward reads them instead of recomputing the
 two full-D reductions, writes ``dv`` and one fp32 ``dw`` partial row per
 consumer group, and a second small kernel sums the rows in a fixed order into
 ``dw`` in ``w``'s dtype -- deterministic, no atomics, no zero-fill launch.
+
+The autograd functions here keep the reference's names and checks; each of
+their forward and backward passes is one call into the PyTorch C++ extension
+``_sy_torch`` (``csrc/torch_ext/sy_torch.cpp``), which allocates the outputs
+with torch's caching allocator on the current stream and launches through the
+C ABI. The remaining entry points go through the ctypes binding ``_native``.
 """
 
 from __future__ import annotations
@@ -27,6 +33,14 @@ from __future__ import annotations
 import torch
 
 from . import _native
+
+try:
+    from . import _sy_torch  # the PyTorch C++ extension over the same C ABI
+except ImportError as exc:  # pragma: no cover - exercised only on a broken install
+    raise ImportError(
+        "switchyard: the C++ extension _sy_torch is missing or stale; build it with "
+        "`python blackwell-switchyard_b200/csrc/build.py` (or __graft_entry__.build())"
+    ) from exc
 
 __all__ = [
     "DEFAULT_EPS",
@@ -60,11 +74,8 @@ def _plan(op: str, n: int, bt: int, d: int, dtype: torch.dtype, s: int = 1) -> i
     return k
 
 
-def _strategy(n: int, bt: int, d: int, dtype: torch.dtype) -> str:
-    return {PLAN_GENERIC: "generic", PLAN_TILE: "register-tile", PLAN_SMEM_TILE: "smem-tile",
-            PLAN_STREAM: "row-stream"}[
-        _plan("fwd", n, bt, d, dtype)
-    ]
+_STRATEGY = {PLAN_GENERIC: "generic", PLAN_TILE: "register-tile", PLAN_SMEM_TILE: "smem-tile",
+             PLAN_STREAM: "row-stream"}
 
 
 def _validate(v: torch.Tensor, w: torch.Tensor) -> None:
@@ -86,51 +97,29 @@ def _validate(v: torch.Tensor, w: torch.Tensor) -> None:
 
 
 def _forward(v: torch.Tensor, w: torch.Tensor, eps: float):
-    """Launch the forward. Returns ``(v, w, out, stats, strategy)`` with ``v``
-    and ``w`` contiguous (the kernels walk tokens with one stride, so B and T
-    are flattened; a contiguous input -- the model's arena alias included --
-    is used in place, never copied)."""
-    n, b, t, d = v.shape
+    """Launch the forward (one call into the C++ extension: allocations on
+    the current stream, ``sy_fwd``). Returns ``(v, w, out, stats, strategy)``
+    with ``v`` and ``w`` contiguous (the kernels walk tokens with one stride,
+    so B and T are flattened; a contiguous input -- the model's arena alias
+    included -- is used in place, never copied)."""
     v = v.contiguous()
     w = w.contiguous()
-    bt = b * t
-    out = torch.empty(b, t, d, device=v.device, dtype=v.dtype)
-    stats = torch.empty(bt, _native.stats_stride(n), device=v.device, dtype=torch.float32)
-    with torch.cuda.device(v.device):
-        if bt > 0 and d > 0:
-            _native.fwd(v, w, out, stats, n, bt, d, eps)
-        strategy = _strategy(n, max(bt, 1), d, v.dtype) if d > 0 else "empty"
-    return v, w, out, stats, strategy
+    out, stats, kind = _sy_torch.forward(v, w, float(eps))
+    return v, w, out, stats, _STRATEGY.get(kind, "empty")
 
 
 def _backward_partials(v, w, stats, grad_out, eps: float):
     """Launch the backward. Returns ``(dv, dw_partial)``: the fp32 partial
     rows of dw, one per CTA (None when D == 0)."""
-    n, b, t, d = v.shape
-    bt = b * t
-    g = grad_out.to(v.dtype).contiguous()
-    dv = torch.empty_like(v)
-    if d == 0:
-        return dv, None
-    with torch.cuda.device(v.device):
-        p = _native.bwd_partials(n, bt, d, v.dtype)
-        part = torch.empty(p, d, device=v.device, dtype=torch.float32)
-        _native.bwd(v, w, g, stats, dv, part, n, bt, d, eps)
+    dv, part = _sy_torch.backward_partials(v, w, stats, grad_out, float(eps))
     return dv, part
 
 
-def _backward(v, w, stats, grad_out, eps: float, dw_dtype: torch.dtype, dw_out=None):
+def _backward(v, w, stats, grad_out, eps: float, dw_dtype: torch.dtype):
     """Launch the backward and the fixed-order dw reduction. Returns
-    ``(dv, dw)`` with ``dw`` in ``dw_dtype`` (float32 for the sharded path,
-    which still has to add the other ranks' contributions), written into
-    ``dw_out`` when one is given."""
-    d = v.shape[-1]
-    dv, part = _backward_partials(v, w, stats, grad_out, eps)
-    dw = torch.empty(d, device=v.device, dtype=dw_dtype) if dw_out is None else dw_out
-    if part is not None:
-        with torch.cuda.device(v.device):
-            _native.dw_reduce(part, dw)
-    return dv, dw
+    ``(dv, dw)`` with ``dw`` in ``dw_dtype`` (float32 for the sharded path's
+    collective exchange, which still adds the other ranks' rows)."""
+    return _sy_torch.backward(v, w, stats, grad_out, float(eps), dw_dtype)
 
 
 class _BlockAttnResTriton(torch.autograd.Function):
@@ -165,15 +154,8 @@ class _BlockAttnResTriton(torch.autograd.Function):
             dv, dw = _backward(v, w, stats, grad_out, ctx.eps, w.dtype)
             return dv, dw, None, None
         v, q, stats, w, gain = ctx.saved_tensors
-        dv, part = _backward_partials(v, q, stats, grad_out, ctx.eps)
-        dw = torch.empty_like(w) if ctx.needs_input_grad[1] else None
-        dg = torch.empty_like(gain) if ctx.needs_input_grad[3] else None
-        if part is None:
-            dw = torch.zeros_like(w) if dw is not None else None
-            dg = torch.zeros_like(gain) if dg is not None else None
-        elif dw is not None or dg is not None:
-            with torch.cuda.device(v.device):
-                _native.dw_reduce_gain(part, w, gain, dw, dg)
+        dv, dw, dg = _sy_torch.backward_gain(v, q, stats, grad_out, w, gain, float(ctx.eps),
+                                             ctx.needs_input_grad[1], ctx.needs_input_grad[3])
         return dv, dw, None, dg
 
 

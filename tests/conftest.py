@@ -4,9 +4,9 @@
   runs with ``-m "not gpu"``);
 * puts the package directory (``blackwell-switchyard_b200/``, not importable by
   name because of the hyphen) and the repository root on ``sys.path``;
-* builds the native library in-tree if it is missing or stale (nvcc
-  cross-compiles for sm_100a without a GPU), so both suites load the real
-  ``libswitchyard_b200.so``.
+* builds the native library and the PyTorch C++ extension in-tree if they are
+  missing or stale (nvcc cross-compiles for sm_100a without a GPU), so both
+  suites load the real ``libswitchyard_b200.so`` and ``_sy_torch.so``.
 """
 
 from __future__ import annotations
@@ -35,6 +35,8 @@ def pytest_configure(config):
         # On a GPU box the library arrives prebuilt; rebuilding there would
         # only happen if a source is newer than it, which nvcc handles too.
         _build.build()
+    if not _build.ext_up_to_date():
+        _build.build_ext()  # the PyTorch C++ extension, linked to the library
 
 
 def golden_cases() -> list[str]:

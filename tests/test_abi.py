@@ -179,10 +179,12 @@ def test_planner_invariants_for_b200(native, dtype_name):
                     assert p["chunks_per_thread"] * p["threads_per_group"] * 16 >= d * dt.itemsize
                     assert p["groups"] * p["threads_per_group"] <= 512 and p["stages"] >= 2
                 if p["kind"] == 3 and op == 1:  # row-stream backward: 4 chunks per lane, exact
-                    assert 2 <= p["threads_per_group"] // 32 <= 16 and n <= 32
+                    kw = p["threads_per_group"] // 32
+                    assert 1 <= kw <= 16 and n <= 64
                     assert p["chunks_per_thread"] * p["threads_per_group"] * 16 == d * dt.itemsize
                     assert p["groups"] * p["threads_per_group"] <= 512 and p["stages"] >= 2
-                    assert p["groups"] <= 8  # named barrier ids 1..8
+                    if kw > 1:
+                        assert p["groups"] <= 15  # named barrier ids 1..15
     # representative forward: re-read row stream, 14 warps x 2 whole tokens each
     # (28 tokens per SM), at least 3 row buffers per warp
     rep = native.plan_info(0, 9, 4096, 2048, 1, torch.bfloat16, **B200)
@@ -199,9 +201,13 @@ def test_planner_invariants_for_b200(native, dtype_name):
         assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw and p["stages"] >= 3
     assert native.plan_info(1, 9, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 1
     # backward rows the register tile cannot hold: the row stream, K = rows / 2 KiB
-    for n, d, kw in ((9, 8192, 8), (17, 4096, 4), (17, 2048, 2)):
+    for n, d, kw in ((9, 8192, 8), (17, 4096, 4), (17, 2048, 2), (33, 2048, 2), (64, 4096, 4),
+                     (33, 8192, 8), (17, 1024, 1), (33, 1024, 1), (64, 1024, 1)):
         p = native.plan_info(1, n, 4096, d, 1, torch.bfloat16, **B200)
-        assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw and p["stages"] >= 3
+        assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw and p["stages"] >= 2, (n, d, p)
+    # the register tile keeps N <= 16 at 2 KiB rows; N = 65 leaves the row stream
+    assert native.plan_info(1, 9, 4096, 1024, 1, torch.bfloat16, **B200)["kind"] == 1
+    assert native.plan_info(1, 65, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] != 3
     # batched queries beyond the register tile: the row-stream batched kernel,
     # K warps per token, as many chunks per lane as the queries' registers allow
     for n, d, s, kw, cpl in ((17, 4096, 8, 8, 2), (20, 2048, 16, 8, 1), (32, 1024, 2, 2, 2),
@@ -213,3 +219,18 @@ def test_planner_invariants_for_b200(native, dtype_name):
         assert p["smem_bytes"] <= B200["max_smem"]
     # rows that are not a multiple of 16 bytes go to the generic kernels
     assert native.plan_info(0, 3, 64, 777, 1, torch.bfloat16, **B200)["kind"] == 0
+
+
+def test_torch_extension_loads_over_the_same_library():
+    """The PyTorch C++ extension (_sy_torch) that the autograd functions call
+    imports on the CPU, exposes its entry points, and uses the same in-tree
+    C-ABI library as the ctypes binding (one copy mapped, not two)."""
+    import torch  # noqa: F401  (the extension links against torch)
+    from switchyard import _native, _sy_torch
+
+    for name in ("forward", "backward_partials", "backward", "backward_gain", "version"):
+        assert hasattr(_sy_torch, name), name
+    assert _sy_torch.version() == _native.version()
+    maps = open("/proc/self/maps").read()
+    mapped = {line.split()[-1] for line in maps.splitlines() if "libswitchyard_b200.so" in line}
+    assert mapped == {str(_native.LIB_PATH.resolve())}, mapped

@@ -430,6 +430,39 @@ def test_row_stream_backward_many_tokens_per_stream(shape, dtype):
     assert O.rel_l2(np64(dw), dw_ref) <= 1.005 * O.dtype_floor(dw_ref, name)
 
 
+@pytest.mark.parametrize("shape,dtype", [
+    ((33, 1, 600, 2048), torch.bfloat16),   # N > 32: two coefficient slots per lane, K = 2
+    ((64, 1, 300, 4096), torch.bfloat16),   # N = 64, the row stream's maximum, K = 4
+    ((33, 1, 900, 1024), torch.bfloat16),   # 2 KiB rows: one warp per token (K = 1)
+    ((17, 2, 700, 1024), torch.float16),    # K = 1 with N <= 32
+    ((40, 1, 500, 512), torch.float32),     # fp32 2 KiB rows, K = 1, two slots
+])
+def test_row_stream_backward_beyond_32_sources_and_2kib_rows(shape, dtype):
+    """The row-stream backward with the per-source coefficients in two
+    register slots per lane (N = 33..64) and with one warp per token (2 KiB
+    rows): dv on sampled tokens and dw over every token against the float64
+    oracle at the dtype's rounding floor, bitwise stable."""
+    n, b, t, d = shape
+    assert _plan("bwd", n, b * t, d, dtype) == PLAN_STREAM
+    name = {torch.bfloat16: "bfloat16", torch.float16: "float16", torch.float32: "float32"}[dtype]
+    v = randn(*shape, dtype=dtype, seed=13)
+    w = randn(d, dtype=dtype, seed=14, scale=d ** -0.5)
+    g = randn(b, t, d, dtype=dtype, seed=15)
+    out, dv, dw = fwd_bwd(v, w, g)
+    _, dv2, dw2 = fwd_bwd(v, w, g)
+    assert torch.equal(dv, dv2) and torch.equal(dw, dw2)
+    toks = torch.randperm(t, generator=torch.Generator().manual_seed(16))[:32].sort().values
+    ww = np64(w)
+    dv_ref, _ = O.backward(np64(v[:, :, toks]), ww, np64(g[:, toks]))
+    floor = (lambda ref: O.dtype_floor(ref, name)) if dtype != torch.float32 else (
+        lambda ref: max(1.6 * O.dtype_floor(ref, name), 1e-6) / 1.005)
+    assert O.rel_l2(np64(dv[:, :, toks]), dv_ref) <= 1.005 * floor(dv_ref)
+    dw_ref = np.zeros(d)
+    for c in range(0, t, 128):
+        dw_ref += O.backward(np64(v[:, :, c:c + 128]), ww, np64(g[:, c:c + 128]))[1]
+    assert O.rel_l2(np64(dw), dw_ref) <= 1.005 * floor(dw_ref)
+
+
 def test_backward_accumulates_dw_in_fp32():
     """tests/test_triton_op.py:185-207: dw over 8192 tokens stays accurate."""
     n, b, t, d = 9, 1, 8192, 512
