@@ -40,6 +40,9 @@
 #ifndef SY_TUNE_BATCHED_REG
 #define SY_TUNE_BATCHED_REG 1  // batched: the register tile where it fits (else row stream)
 #endif
+#ifndef SY_TUNE_BWD_L2_PCT
+#define SY_TUNE_BWD_L2_PCT 0  // row-stream backward: % of L2 its rows in flight may fill (0: no cap)
+#endif
 
 namespace sy {
 
@@ -53,7 +56,12 @@ constexpr int kMaxDevices = 64;
 struct DevInfo {
   int sms = 0;
   int max_smem = 0;  // opt-in dynamic shared memory per block
+  int64_t l2 = 0;    // L2 bytes
 };
+
+// L2 assumed by sy_plan_info when it is given a device's SM count and shared
+// memory instead of querying one (B200: 126 MiB).
+constexpr int64_t kAssumedL2Bytes = int64_t(126) << 20;
 
 cudaError_t dev_info(DevInfo* out) {
   static std::mutex mu;
@@ -69,6 +77,10 @@ cudaError_t dev_info(DevInfo* out) {
     if (e != cudaSuccess) return e;
     e = cudaDeviceGetAttribute(&d.max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e != cudaSuccess) return e;
+    int l2 = 0;
+    e = cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev);
+    if (e != cudaSuccess) return e;
+    d.l2 = l2;
     cache[dev] = d;
   }
   *out = cache[dev];
@@ -329,7 +341,15 @@ StreamBwdPlan plan_stream_bwd(int64_t N, int64_t BT, int64_t D, int dtype, const
   if (rc % per_warp) return p;
   const int64_t kw = rc / per_warp;
   if (kw < 1 || kw > 16) return p;
-  const int64_t max_streams = kStreamBwdThreads / 32 / kw;
+  int64_t max_streams = kStreamBwdThreads / 32 / kw;
+  // Pass B reads each row of a token again from L2; between its two reads a
+  // token stream reads the token's other N rows, so the rows in flight are
+  // streams x SMs x N rows. Keep them within SY_TUNE_BWD_L2_PCT % of L2 (at
+  // N = 33, 4 KiB rows, 7 streams per SM hold 137 MB: the re-read missed L2).
+  if (SY_TUNE_BWD_L2_PCT > 0 && di.l2 > 0) {
+    const int64_t fit = (int64_t)SY_TUNE_BWD_L2_PCT * di.l2 / 100 / ((int64_t)di.sms * N * (D * es));
+    if (fit < max_streams) max_streams = fit < 1 ? 1 : fit;
+  }
   const int64_t g0 = BT < di.sms ? BT : di.sms;
   const int64_t t = (BT + g0 - 1) / g0;                // tokens per CTA
   const int64_t k = (t + max_streams - 1) / max_streams;  // tokens per stream
@@ -878,6 +898,7 @@ int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype,
   if (sms > 0 && max_smem > 0) {
     di.sms = sms;
     di.max_smem = max_smem;
+    di.l2 = kAssumedL2Bytes;
   } else {
     const cudaError_t e = dev_info(&di);
     if (e != cudaSuccess) return cuda_status(e, "sy_plan_info: device query");

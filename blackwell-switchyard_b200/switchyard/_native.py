@@ -49,9 +49,9 @@ SIGNATURES: dict[str, tuple[list, object]] = {
     "sy_device_error": ([_c.POINTER(_c.c_int)], _I),
     "sy_bwd_noalloc": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I, _I, _F, _P], _I),
     "sy_bwd_noalloc_max_floats": ([], _I64),
-    "sy_dw_exchange": ([_P, _I64, _I64, _P, _I, _I, _I64, _I64, _c.c_uint32, _P, _I,
+    "sy_dw_exchange": ([_P, _I64, _I64, _P, _I, _I, _I64, _c.c_uint32, _P, _I,
                         _c.c_uint64, _P, _P, _P], _I),
-    "sy_dw_exchange_flags": ([_I64, _I], _I64),
+    "sy_dw_exchange_bytes": ([_I64, _I], _I64),
 }
 
 
@@ -245,16 +245,16 @@ def device_error() -> int:
     return code.value
 
 
-def dw_exchange_flags(length: int, world: int) -> int:
-    n = int(lib.sy_dw_exchange_flags(length, world))
+def dw_exchange_bytes(length: int, world: int) -> int:
+    n = int(lib.sy_dw_exchange_bytes(length, world))
     if n < 0:
-        raise NativeError("sy_dw_exchange_flags", -n)
+        raise NativeError("sy_dw_exchange_bytes", -n)
     return n
 
 
-def dw_exchange(part, peer_bases, world: int, rank: int, slot_off: int, flag_off: int, tag: int,
-                dw, wait_limit_ns: int = 0, timing=None, fail_word=None) -> None:
-    """Sum this rank's fp32 partial rows ``part`` [P, L] and every rank's slot
+def dw_exchange(part, peer_bases, world: int, rank: int, buf_off: int, tag: int, dw,
+                wait_limit_ns: int = 0, timing=None, fail_word=None) -> None:
+    """Sum this rank's fp32 partial rows ``part`` [P, L] and every rank's rows
     in rank order into ``dw`` [L] (sy_dw_exchange); ``peer_bases`` is a CUDA
     int64 tensor of the ranks' buffer addresses, ``timing`` an optional CUDA
     int64 tensor of 8 counters, ``fail_word`` an optional device-visible int32
@@ -263,8 +263,8 @@ def dw_exchange(part, peer_bases, world: int, rank: int, slot_off: int, flag_off
     p, length = part.shape
     check(
         lib.sy_dw_exchange(part.data_ptr(), p, length, peer_bases.data_ptr(), world, rank,
-                           slot_off, flag_off, tag & 0xFFFFFFFF, dw.data_ptr(),
-                           dtype_code(dw.dtype), int(wait_limit_ns),
+                           buf_off, tag & 0xFFFFFFFF, dw.data_ptr(), dtype_code(dw.dtype),
+                           int(wait_limit_ns),
                            timing.data_ptr() if timing is not None else None,
                            fail_word.data_ptr() if fail_word is not None else None,
                            stream_of(dw)),

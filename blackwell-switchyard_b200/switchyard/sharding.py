@@ -10,12 +10,13 @@ own fp32 partial and every rank adds all ranks' partials in rank order
 0..world-1, so all ranks hold the bitwise-same ``dw`` and the result is
 deterministic for a given partition.
 
-On CUDA ranks the partials cross NVLink as peer loads: one kernel
+On CUDA ranks the partials cross NVLink as peer stores: one kernel
 (``sy_dw_exchange``), launched as a programmatic dependent of the backward,
-sums the rank's partial rows into a buffer every rank can address (torch
-symmetric memory, allocated once per group and D), announces each 32-column
-block to every rank, waits for all ranks with a bounded wait, and adds the
-peers' rows directly -- no NCCL call and no second launch on the step.
+sums the rank's partial rows and stores each column, with the call's tag in
+the same 8-byte word, into every other rank's buffer (torch symmetric memory,
+allocated once per group and D); each rank waits, bounded, for the others'
+words in its own memory and adds all ranks' rows in rank order -- no NCCL call
+and no second launch on the step.
 Elsewhere (gloo on CPU, or if peer memory is not available, or with
 ``SWITCHYARD_DW_EXCHANGE=collective``) the rows are all-gathered with the
 process group and summed in the same order, which gives the same bits.
@@ -75,14 +76,15 @@ class PeerExchangeError(RuntimeError):
 
 class PeerExchange:
     """The peer-memory gradient exchange of one (process group, length L,
-    device): a buffer every rank can address -- two fp32 slots of L floats,
-    used alternately, and one uint32 flag per (rank, 32-column block) -- and the
-    device array of all ranks' addresses of it. Built collectively on first
-    use (:func:`peer_exchange`).
+    device): a buffer every rank can address -- two slots, used alternately, of
+    one 8-byte (value, tag) word per (source rank, column) -- and the device
+    array of all ranks' addresses of it. Built collectively on first use
+    (:func:`peer_exchange`).
 
     :meth:`reduce_exchange` is one launch (``sy_dw_exchange``): it sums this
-    rank's partial rows in ``sy_dw_reduce``'s order, publishes them, waits for
-    every rank (bounded) and adds all ranks' sums in rank order.
+    rank's partial rows in ``sy_dw_reduce``'s order, stores them into every
+    other rank's buffer, waits in its own buffer for every rank's words
+    (bounded) and adds all ranks' sums in rank order.
 
     Failure handling: if a wait runs out, that call's output is NaN and its tag
     lands in :attr:`fail` (pinned host memory the kernel writes, read by the
@@ -100,24 +102,21 @@ class PeerExchange:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.length = length
-        self.slot_floats = (length + 3) // 4 * 4  # keeps the second slot 16-byte aligned
-        nflags = _native.dw_exchange_flags(length, self.world)
-        flag_floats = (nflags + 3) // 4 * 4
-        self.buf = symm.empty(2 * self.slot_floats + flag_floats, dtype=torch.float32,
-                              device=device)
+        nbytes = _native.dw_exchange_bytes(length, self.world)
+        self.buf = symm.empty(nbytes // 8, dtype=torch.int64, device=device)
         self.buf.zero_()
         self.handle = symm.rendezvous(self.buf, group)
         ptrs = list(self.handle.buffer_ptrs)
         delta = self.buf.data_ptr() - ptrs[self.rank]
         self.bases = torch.tensor([p + delta for p in ptrs], dtype=torch.int64, device=device)
-        self.flag_off = 2 * self.slot_floats * 4
+        self.calls = 0
         self.tag = 0
         self.wait_limit_ns = EXCHANGE_WAIT_LIMIT_NS
         self.fail = torch.zeros(1, dtype=torch.int32, pin_memory=True)
         self.timing = None
         self.broken = None
         torch.cuda.synchronize(device)
-        dist.barrier(group)  # every rank's flags are zero before the first announcement
+        dist.barrier(group)  # every rank's buffer is zero before the first words arrive
 
     def check(self) -> None:
         """Raise if an earlier call of this exchange timed out (host read of the
@@ -135,10 +134,12 @@ class PeerExchange:
         """``out`` [L] (any of the three dtypes) = sum over ranks, in rank
         order, of each rank's fp32 sum of its partial rows ``part`` [P, L]."""
         self.check()
-        self.tag += 1
-        slot_off = (self.tag & 1) * self.slot_floats * 4
-        _native.dw_exchange(part, self.bases, self.world, self.rank, slot_off, self.flag_off,
-                            self.tag, out, self.wait_limit_ns, self.timing, self.fail)
+        self.calls += 1
+        # 1, 2, ..., 2**32 - 2, 1, ...: never 0 (the zeroed buffer's tag), and
+        # the parity, which picks the slot, alternates across the wrap too
+        self.tag = (self.calls - 1) % (2**32 - 2) + 1
+        _native.dw_exchange(part, self.bases, self.world, self.rank, 0, self.tag, out,
+                            self.wait_limit_ns, self.timing, self.fail)
 
     def start_timing(self) -> None:
         """Count calls and phase nanoseconds from now on (device counters)."""

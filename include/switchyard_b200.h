@@ -259,40 +259,38 @@ SY_API int64_t sy_bwd_noalloc_max_floats(void);
  * dw_partial: this rank's [P, L] fp32 partial rows (sy_bwd's dw_partial, L = D;
  * or sy_bwd_batched's, L = S * D), written by earlier work on `stream` (the
  * kernel is a programmatic dependent launch of it).
- * Every rank owns a buffer that all ranks can address (NVLink peer mappings)
- * holding two fp32 slots of L floats -- slot_off selects slot `tag & 1` -- and
- * sy_dw_exchange_flags(L, world) uint32 flags at flag_off, all zero before the
- * first call; peer_bases is a DEVICE array of `world` 64-bit addresses, entry r
- * = rank r's buffer base. The kernel sums the rank's rows in sy_dw_reduce's
- * order into its own slot, announces `tag` per 32-column block to every rank,
- * waits for all ranks' announcements of the block (bounded by wait_limit_ns;
- * 0 means 2 s), then writes dw[L] in dw_dtype = sum over ranks 0..world-1, in
- * that order, of their slots -- bitwise the same on every rank, and bitwise an
- * all-gather of the ranks' sy_dw_reduce results added in rank order in fp32.
- * Tags must increase by one per call, the same sequence on every rank.
+ * Every rank owns a buffer that all ranks can address (NVLink peer mappings) of
+ * sy_dw_exchange_bytes(L, world) bytes at byte offset buf_off (8-byte aligned)
+ * from its base, zeroed before the first call; peer_bases is a DEVICE array of
+ * `world` 64-bit addresses, entry r = rank r's buffer base. The kernel sums the
+ * rank's rows in sy_dw_reduce's order, stores each column as one 8-byte word
+ * (fp32 value, tag) into every other rank's buffer, waits in its own buffer for
+ * every other rank's words of this tag (bounded by wait_limit_ns; 0 means 2 s),
+ * then writes dw[L] in dw_dtype = sum over ranks 0..world-1, in that order --
+ * bitwise the same on every rank, and bitwise an all-gather of the ranks'
+ * sy_dw_reduce results added in rank order in fp32. Tags start at 1 and
+ * increase by one per call, the same sequence on every rank.
  *
  * A wait that runs out does not hang: the block's dw values are NaN, the
  * device error word gets bit 1 (sy_device_error) and, if fail_word is not
  * NULL, the tag is stored there (any device-visible memory; mapped pinned host
  * memory lets the host see it without a synchronisation). timing, if not NULL,
  * is 8 device uint64 counters that block 0 adds to on every call: calls; total
- * and largest nanoseconds from its announcement to the last peer's flag; total
+ * and largest nanoseconds from its pushes to the last peer word; total
  * nanoseconds from the kernel's start to the end of its sum; then the totals of
- * its phases: the partial-row sum, the slot store and announcement, the peer
- * reads and the output store (the eighth is unused). Plain peer loads and
- * stores only (no multicast).
+ * its phases: the partial-row sum, the pushes, the wait with the rank-order sum
+ * and the output store (the eighth is unused). Plain peer stores and local
+ * loads only (no multicast).
  */
 SY_API int sy_dw_exchange(const float* dw_partial, int64_t P, int64_t L,
-                          const void* peer_bases, int world, int rank,
-                          int64_t slot_off, int64_t flag_off, uint32_t tag,
-                          void* dw, int dw_dtype, uint64_t wait_limit_ns,
+                          const void* peer_bases, int world, int rank, int64_t buf_off,
+                          uint32_t tag, void* dw, int dw_dtype, uint64_t wait_limit_ns,
                           unsigned long long* timing, unsigned int* fail_word,
                           sy_stream_t stream);
 
-/* Number of uint32 flags sy_dw_exchange uses per rank buffer for L columns
- * and `world` ranks: world * ceil(L / 32), or -status. No reference
- * counterpart. */
-SY_API int64_t sy_dw_exchange_flags(int64_t L, int world);
+/* Bytes of each rank's sy_dw_exchange buffer for L columns and `world` ranks:
+ * two slots of world * L 8-byte words, or -status. No reference counterpart. */
+SY_API int64_t sy_dw_exchange_bytes(int64_t L, int world);
 
 /*
  * Reads the device-side error word of the current device and clears it.

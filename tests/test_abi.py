@@ -84,29 +84,30 @@ def test_host_validation_rejects_bad_arguments(native):
     assert L.sy_dw_reduce(None, 1, 0, None, bf16, None) == native.SY_OK
     assert L.sy_bwd_partials(3, 0, 16, bf16) == 1
     assert L.sy_bwd_partials(0, 4, 16, bf16) < 0
-    # dw exchange (part, P, L, bases, world, rank, slot_off, flag_off, tag, dw, dtype,
-    # limit, timing, fail, stream): rank outside the world, misaligned offsets,
-    # bad world size, no partial rows, dtype, misaligned timing counters
-    def ex(part=1, p=4, length=8, bases=1, world=2, rank=0, slot=0, flag=64, dw=1,
-           dtype=bf16, timing=None):
-        return L.sy_dw_exchange(part, p, length, bases, world, rank, slot, flag, 1, dw, dtype, 0,
+    # dw exchange (part, P, L, bases, world, rank, buf_off, tag, dw, dtype, limit, timing,
+    # fail, stream): rank outside the world, misaligned offset, bad world size, no
+    # partial rows, tag 0, dtype, misaligned timing counters
+    def ex(part=1, p=4, length=8, bases=1, world=2, rank=0, off=0, tag=1, dw=1, dtype=bf16,
+           timing=None):
+        return L.sy_dw_exchange(part, p, length, bases, world, rank, off, tag, dw, dtype, 0,
                                 timing, None, None)
 
     assert ex(rank=2) == native.SY_ERR_ARG
-    assert ex(slot=6) == native.SY_ERR_ARG
-    assert ex(flag=66) == native.SY_ERR_ARG
+    assert ex(off=4) == native.SY_ERR_ARG
+    assert ex(off=-8) == native.SY_ERR_ARG
     assert ex(world=0) == native.SY_ERR_ARG
     assert ex(world=65, rank=0) == native.SY_ERR_ARG
     assert ex(p=0) == native.SY_ERR_ARG
+    assert ex(tag=0) == native.SY_ERR_ARG
     assert ex(dtype=bad) == native.SY_ERR_DTYPE
     assert ex(timing=12) == native.SY_ERR_ARG
     assert ex(bases=None) == native.SY_ERR_ARG
     assert ex(part=None, bases=None, dw=None, length=0) == native.SY_OK
-    # flags per rank buffer: world x 32-column blocks
-    assert L.sy_dw_exchange_flags(2048, 8) == 8 * 64
-    assert L.sy_dw_exchange_flags(33, 2) == 4
-    assert L.sy_dw_exchange_flags(0, 3) == 0
-    assert L.sy_dw_exchange_flags(8, 0) < 0
+    # bytes per rank buffer: two slots of world x L 8-byte words
+    assert L.sy_dw_exchange_bytes(2048, 8) == 2 * 8 * 2048 * 8
+    assert L.sy_dw_exchange_bytes(33, 2) == 2 * 2 * 33 * 8
+    assert L.sy_dw_exchange_bytes(0, 3) == 0
+    assert L.sy_dw_exchange_bytes(8, 0) < 0
     # gain-split dw reduction: dtype, null inputs, nothing to write, empty D
     assert L.sy_dw_reduce_gain(1, 4, 8, 1, 1, 1, 1, bad, None) == native.SY_ERR_DTYPE
     assert L.sy_dw_reduce_gain(1, 4, 8, None, 1, 1, 1, bf16, None) == native.SY_ERR_ARG

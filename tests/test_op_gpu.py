@@ -219,7 +219,8 @@ EPS_SHAPES = [  # fp32 shapes that reach every kernel family
     ((17, 1, 40, 1024), PLAN_STREAM, PLAN_STREAM),  # backward: 2 warps per token
     ((10, 1, 24, 2048), PLAN_STREAM, PLAN_STREAM),  # 8 KiB rows: split row streams
     ((10, 1, 24, 1536), PLAN_SMEM_TILE, PLAN_STREAM),  # backward: 3 warps per token
-    ((33, 1, 24, 512), PLAN_STREAM, PLAN_SMEM_TILE),
+    ((33, 1, 24, 512), PLAN_STREAM, PLAN_STREAM),  # backward: 1 warp per token, N > 32
+    ((33, 1, 24, 768), PLAN_STREAM, PLAN_SMEM_TILE),  # 3 KiB rows: the shared-memory tile
     ((3, 1, 16, 777), PLAN_GENERIC, PLAN_GENERIC),
 ]
 
