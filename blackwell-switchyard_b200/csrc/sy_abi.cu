@@ -41,7 +41,7 @@
 #define SY_TUNE_BATCHED_REG 1  // batched: the register tile where it fits (else row stream)
 #endif
 #ifndef SY_TUNE_BWD_L2_PCT
-#define SY_TUNE_BWD_L2_PCT 0  // row-stream backward: % of L2 its rows in flight may fill (0: no cap)
+#define SY_TUNE_BWD_L2_PCT 0  // row-stream backward: fit rows in flight in this % of L2 (0: off)
 #endif
 
 namespace sy {
@@ -325,10 +325,18 @@ struct StreamBwdPlan {
   int64_t smem = 0;
 };
 
-// Row-stream backward: rows of exactly 128 * K chunks, K = 1 .. 16 warps per
-// token (2 .. 32 KiB rows at 2 bytes per element), N <= 64. Whole tokens per
-// token stream, as evenly as possible (as the forward's re-read stream). It
-// runs where the register tile does not (N > 16, or rows over 4 KiB).
+// Row-stream backward: rows of exactly 32 * CPL * K chunks (CPL = 4, 2 or 1
+// chunks per lane, K = 1 .. 16 warps per token), N <= 64; it runs where the
+// register tile does not (N > 16, or rows over 4 KiB). Whole tokens per token
+// stream, as evenly as possible (as the forward's re-read stream). The most
+// chunks per lane that divide the row: fewer warps per token, fewer barriers.
+// Pass B re-reads each row, normally from L2, but the rows in flight (token
+// streams x SMs x N rows) can exceed L2 at large N (N = 33, 4 KiB rows: 137 MB).
+// Two ways of keeping them within L2 were measured and are slower at every
+// shape tried (N = 17..64, D = 1024..8192): fewer token streams (0.67 -> 0.15-0.52
+// of the copy peak at N = 33 D = 2048) and fewer chunks per lane with more warps
+// per token (0.67 -> 0.53); the DRAM re-reads cost less than either.
+// SY_TUNE_BWD_L2_PCT > 0 keeps the second rule for experiments.
 StreamBwdPlan plan_stream_bwd(int64_t N, int64_t BT, int64_t D, int dtype, const DevInfo& di) {
   StreamBwdPlan p;
   const int es = esize_of(dtype);
@@ -337,29 +345,29 @@ StreamBwdPlan plan_stream_bwd(int64_t N, int64_t BT, int64_t D, int dtype, const
     return p;
   if ((D * es) % 16) return p;
   const int64_t rc = D * es / 16;
-  const int64_t per_warp = 32 * kStreamBwdCpl;
-  if (rc % per_warp) return p;
-  const int64_t kw = rc / per_warp;
-  if (kw < 1 || kw > 16) return p;
-  int64_t max_streams = kStreamBwdThreads / 32 / kw;
-  // Pass B reads each row of a token again from L2; between its two reads a
-  // token stream reads the token's other N rows, so the rows in flight are
-  // streams x SMs x N rows. Keep them within SY_TUNE_BWD_L2_PCT % of L2 (at
-  // N = 33, 4 KiB rows, 7 streams per SM hold 137 MB: the re-read missed L2).
-  if (SY_TUNE_BWD_L2_PCT > 0 && di.l2 > 0) {
-    const int64_t fit = (int64_t)SY_TUNE_BWD_L2_PCT * di.l2 / 100 / ((int64_t)di.sms * N * (D * es));
-    if (fit < max_streams) max_streams = fit < 1 ? 1 : fit;
-  }
   const int64_t g0 = BT < di.sms ? BT : di.sms;
-  const int64_t t = (BT + g0 - 1) / g0;                // tokens per CTA
-  const int64_t k = (t + max_streams - 1) / max_streams;  // tokens per stream
-  const int64_t streams = (t + k - 1) / k;
-  if (k * (2 * N + 1) >= (int64_t)INT_MAX) return p;  // stream rows are counted in 32 bits
+  const int64_t t = (BT + g0 - 1) / g0;  // tokens per CTA
+  const int64_t budget = di.l2 > 0 ? (int64_t)SY_TUNE_BWD_L2_PCT * di.l2 / 100 : 0;
+  int64_t kw = 0, streams = 0, cpl = 0;
+  for (int64_t c = kStreamBwdMaxCpl; c >= 1; c /= 2) {
+    if (rc % (32 * c)) continue;
+    const int64_t k_w = rc / (32 * c);
+    if (k_w < 1 || k_w > 16) continue;
+    int64_t max_streams = kStreamBwdThreads / 32 / k_w;
+    if (k_w > 1 && max_streams > 15) max_streams = 15;  // named barrier ids 1..15
+    const int64_t k = (t + max_streams - 1) / max_streams;  // tokens per stream
+    const int64_t s = (t + k - 1) / k;
+    if (k * (2 * N + 1) >= (int64_t)INT_MAX) continue;  // stream rows are counted in 32 bits
+    kw = k_w, streams = s, cpl = c;
+    if (budget == 0 || s * di.sms * N * (D * es) <= budget) break;
+  }
+  if (!cpl) return p;
   StreamBwdCfg c{};
   c.BT = BT;
   c.N = (int)N;
   c.D = (int)D;
   c.row_chunks = (int)rc;
+  c.cpl = (int)cpl;
   c.row_bytes = (int)(D * es);
   c.kw = (int)kw;
   c.warps = (int)(streams * kw);
@@ -931,7 +939,7 @@ int sy_plan_info(int op, int64_t N, int64_t BT, int64_t D, int64_t S, int dtype,
       out[2] = sb.c.ring;
       out[3] = sb.c.warps / sb.c.kw;  // token streams per CTA
       out[4] = 32 * sb.c.kw;          // threads per token stream
-      out[5] = kStreamBwdCpl;
+      out[5] = sb.c.cpl;
       out[6] = sb.c.row_bytes;
       out[7] = sb.smem;
       return SY_OK;

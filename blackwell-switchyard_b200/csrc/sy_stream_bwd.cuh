@@ -2,8 +2,9 @@
 //
 // The register-tile backward holds a token's N source rows in registers; at
 // 16 KiB rows (D = 8192 bf16) or N > 16 they no longer fit. Here K warps share
-// each token (K = 1 .. 16: rows of 2 to 32 KiB at two bytes per element), warp
-// k owning chunks 128k .. 128k+127 of every row (4 per lane),
+// each token (K = 1 .. 16), warp k owning chunks 32 CPL k .. 32 CPL (k+1) - 1 of
+// every row (CPL = 1, 2 or 4 per lane: more warps per token for the same row
+// keep fewer tokens in flight, see the planner),
 // and the token's rows stream through the K warps' shared ring of R row
 // buffers (cp.async.bulk, one mbarrier per buffer) in the order
 //
@@ -42,7 +43,8 @@ namespace sy {
 struct StreamBwdCfg {
   long long BT;
   int N, D;
-  int row_chunks;  // 16-byte chunks per row: exactly 128 * kw
+  int row_chunks;  // 16-byte chunks per row: exactly 32 * cpl * kw
+  int cpl;         // 16-byte chunks per lane and row: 1, 2 or 4
   int row_bytes;
   int kw;          // warps per token
   int warps;       // per CTA, a multiple of kw
@@ -77,8 +79,8 @@ __host__ __device__ inline StreamBwdSmem stream_bwd_smem_layout(const StreamBwdC
 #define SY_TUNE_STREAM_BWD_WARPS 16
 #endif
 constexpr int kStreamBwdThreads = 32 * SY_TUNE_STREAM_BWD_WARPS;
-constexpr int kStreamBwdCpl = 4;   // 16-byte chunks per lane and row
-constexpr int kStreamBwdMaxN = 64;  // lane n % 32, register slot n / 32, holds source n
+constexpr int kStreamBwdMaxCpl = 4;  // 16-byte chunks per lane and row: 1, 2 or 4
+constexpr int kStreamBwdMaxN = 64;    // lane n % 32, register slot n / 32, holds source n
 
 // L2 hint for pass A's copy of a row (pass B reads it again).
 #ifndef SY_TUNE_STREAM_BWD_KEEP
@@ -86,12 +88,12 @@ constexpr int kStreamBwdMaxN = 64;  // lane n % 32, register slot n / 32, holds 
 #endif
 
 // SL: register slots of per-source coefficients per lane (1: N <= 32, 2: N <= 64).
-template <typename T, int SL>
+// CPL: 16-byte chunks per lane and row (a row is K warps x 32 lanes x CPL).
+template <typename T, int SL, int CPL>
 __global__ void __launch_bounds__(kStreamBwdThreads, 1)
     stream_bwd_kernel(const T* __restrict__ v, const void* __restrict__ w, int w_dtype,
                       const T* __restrict__ gin, const float* __restrict__ stats,
                       T* __restrict__ dv, float* __restrict__ dw_partial, const StreamBwdCfg c) {
-  constexpr int CPL = kStreamBwdCpl;
   constexpr int VEC = Dt<T>::kVec;
   constexpr int P = VEC / 2;
   const StreamBwdSmem L = stream_bwd_smem_layout(c);
@@ -108,7 +110,7 @@ __global__ void __launch_bounds__(kStreamBwdThreads, 1)
   const int RC = c.row_chunks;
   const int RB = c.row_bytes;
   if (K < 1 || K > 16 || c.warps % K != 0 || c.warps != (int)(blockDim.x >> 5) || c.ring < 2 ||
-      RC != 32 * CPL * K || RB != 16 * RC || c.N < 1 || c.N > 32 * SL ||
+      c.cpl != CPL || RC != 32 * CPL * K || RB != 16 * RC || c.N < 1 || c.N > 32 * SL ||
       (K > 1 && c.warps / K > 15)) {
     if (tid == 0) record_device_error(kDevErrBadPlan);
     return;

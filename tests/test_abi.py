@@ -202,10 +202,14 @@ def test_planner_invariants_for_b200(native, dtype_name):
         assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw and p["stages"] >= 3
     assert native.plan_info(1, 9, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] == 1
     # backward rows the register tile cannot hold: the row stream, K = rows / 2 KiB
-    for n, d, kw in ((9, 8192, 8), (17, 4096, 4), (17, 2048, 2), (33, 2048, 2), (64, 4096, 4),
-                     (33, 8192, 8), (17, 1024, 1), (33, 1024, 1), (64, 1024, 1)):
+    # (chunks per lane, warps per token): the most chunks per lane (4, 2, 1)
+    # that divide the row, then K = row chunks / (32 x chunks per lane)
+    for n, d, cpl, kw in ((9, 8192, 4, 8), (17, 4096, 4, 4), (17, 2048, 4, 2), (33, 2048, 4, 2),
+                          (64, 4096, 4, 4), (33, 8192, 4, 8), (17, 1024, 4, 1), (33, 1024, 4, 1),
+                          (64, 1024, 4, 1), (17, 1536, 2, 3), (20, 1280, 1, 5)):
         p = native.plan_info(1, n, 4096, d, 1, torch.bfloat16, **B200)
-        assert p["kind"] == 3 and p["threads_per_group"] == 32 * kw and p["stages"] >= 2, (n, d, p)
+        assert p["kind"] == 3 and p["stages"] >= 2, (n, d, p)
+        assert (p["chunks_per_thread"], p["threads_per_group"] // 32) == (cpl, kw), (n, d, p)
     # the register tile keeps N <= 16 at 2 KiB rows; N = 65 leaves the row stream
     assert native.plan_info(1, 9, 4096, 1024, 1, torch.bfloat16, **B200)["kind"] == 1
     assert native.plan_info(1, 65, 4096, 2048, 1, torch.bfloat16, **B200)["kind"] != 3

@@ -220,7 +220,8 @@ EPS_SHAPES = [  # fp32 shapes that reach every kernel family
     ((10, 1, 24, 2048), PLAN_STREAM, PLAN_STREAM),  # 8 KiB rows: split row streams
     ((10, 1, 24, 1536), PLAN_SMEM_TILE, PLAN_STREAM),  # backward: 3 warps per token
     ((33, 1, 24, 512), PLAN_STREAM, PLAN_STREAM),  # backward: 1 warp per token, N > 32
-    ((33, 1, 24, 768), PLAN_STREAM, PLAN_SMEM_TILE),  # 3 KiB rows: the shared-memory tile
+    ((33, 1, 24, 768), PLAN_STREAM, PLAN_STREAM),  # 3 KiB rows: 2 chunks per lane, 3 warps
+    ((33, 1, 24, 648), PLAN_STREAM, PLAN_SMEM_TILE),  # 162 chunks a row: the shared-memory tile
     ((3, 1, 16, 777), PLAN_GENERIC, PLAN_GENERIC),
 ]
 
@@ -437,6 +438,8 @@ def test_row_stream_backward_many_tokens_per_stream(shape, dtype):
     ((33, 1, 900, 1024), torch.bfloat16),   # 2 KiB rows: one warp per token (K = 1)
     ((17, 2, 700, 1024), torch.float16),    # K = 1 with N <= 32
     ((40, 1, 500, 512), torch.float32),     # fp32 2 KiB rows, K = 1, two slots
+    ((17, 1, 400, 1536), torch.bfloat16),   # 3 KiB rows: 2 chunks per lane, K = 3
+    ((20, 1, 300, 1280), torch.bfloat16),   # 2.5 KiB rows: 1 chunk per lane, K = 5
 ])
 def test_row_stream_backward_beyond_32_sources_and_2kib_rows(shape, dtype):
     """The row-stream backward with the per-source coefficients in two
