@@ -51,9 +51,9 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import _native
+from . import _sy_torch
 from .arena import stage_partial
-from .triton_op import DEFAULT_EPS, _backward_partials, _BlockAttnResTriton, _forward
+from .triton_op import DEFAULT_EPS, _BlockAttnResTriton, _forward
 
 __all__ = [
     "DecoderConfig",
@@ -287,14 +287,9 @@ class _ArenaSite(torch.autograd.Function):
         if ctx.fused:
             q, stats, w, g = saved[:4]
             v = arena_alias(ctx.arena, ctx.n_src)
-            dv, part = _backward_partials(v, q, stats, grad_out, ctx.eps)
-            dw, dg = torch.empty_like(w), torch.empty_like(g)
-            if part is None:
-                dw.zero_()
-                dg.zero_()
-            else:
-                with torch.cuda.device(v.device):
-                    _native.dw_reduce_gain(part, w, g, dw, dg)
+            # one extension call: backward kernel, then the gain-split reduction
+            dv, dw, dg = _sy_torch.backward_gain(v, q, stats, grad_out, w, g, float(ctx.eps),
+                                                 True, True)
         else:
             vv, ww, gg, out = ctx.inner
             ctx.inner = None
