@@ -142,7 +142,7 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80,
     }
 
-    def __init__(self, device_index: int, period_s: float = 0.005):
+    def __init__(self, device_index: int, period_s: float = 0.002):
         self.ok = False
         self.samples = []
         self.reasons = set()
@@ -168,23 +168,27 @@ class ClockSampler:
         except Exception as exc:  # noqa: BLE001
             self.err = str(exc)
 
-    def _run(self):
+    def _sample(self):
         nv = self.nv
+        try:
+            self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+            get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or getattr(
+                nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+            mask = get(self.h)
+            for name, bit in self.REASONS.items():
+                if mask & bit:
+                    self.reasons.add(name)
+        except Exception:  # noqa: BLE001
+            pass
+
+    def _run(self):
         while not self._stop.is_set():
-            try:
-                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
-                get = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or getattr(
-                    nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
-                mask = get(self.h)
-                for name, bit in self.REASONS.items():
-                    if mask & bit:
-                        self.reasons.add(name)
-            except Exception:  # noqa: BLE001
-                pass
+            self._sample()
             time.sleep(self.period)
 
     def __enter__(self):
         if self.ok:
+            self._sample()  # one at the start, whatever the thread's start-up delay
             self.t = threading.Thread(target=self._run, daemon=True)
             self.t.start()
         return self
@@ -223,13 +227,14 @@ class L2Flush:
         torch.sum(self.r, dim=0, out=self.o)
 
 
-def timed_steps(fn, steps, flush, lead_cycles=2_000_000, align=None):
+def timed_steps(fn, steps, flush, lead_cycles=2_000_000, align=None, on_queued=None):
     """Per-step device times (ms): flush L2, let a spin kernel cover the host's
     queueing of the step, then bracket only the step with CUDA events on the
     current stream. ``align`` (multi-GPU) queues a device-side barrier across
     the ranks' streams after the spin kernel, so every rank's step starts at
     the same moment and no rank's events include another rank's flush or
-    host jitter."""
+    host jitter. ``on_queued`` runs once every step is queued, while the GPU
+    works through them (the clock sampler takes a sample there)."""
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
     for i in range(steps):
@@ -240,6 +245,8 @@ def timed_steps(fn, steps, flush, lead_cycles=2_000_000, align=None):
         starts[i].record()
         fn()
         ends[i].record()
+    if on_queued is not None:
+        on_queued()  # the steps are queued and running: a sample inside the timed region
     torch.cuda.synchronize()
     return [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
@@ -714,7 +721,8 @@ def run_ours(args):
         peer.start_timing()
     torch.cuda.synchronize()
     with sampler:
-        step_ms = timed_steps(step, args.steps, flush, align=align)
+        step_ms = timed_steps(step, args.steps, flush, align=align, on_queued=sampler._sample
+                              if sampler.ok else None)
     torch.cuda.synchronize()
     exch = None
     if world > 1:
