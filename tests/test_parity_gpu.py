@@ -136,7 +136,13 @@ def test_backward_other_dtypes(shape, dtype):
      # the row-stream batched kernel: several tokens per stream, S = 16 (32-wide
      # reduce-scatter), S = 9 (two sweeps of pass B), N up to 32
      ((20, 1, 300, 2048), 16), ((17, 1, 200, 4096), 3), ((24, 1, 160, 1024), 9),
-     ((32, 2, 80, 1024), 2)],
+     ((32, 2, 80, 1024), 2),
+     # the register-tile batched kernel at its edges: one source, N = 8 and 16,
+     # 9 to 16 queries (three and six query blocks), 128-column rows, several
+     # tokens per group around the ring, 8 KiB rows
+     ((1, 1, 9, 64), 3), ((8, 1, 40, 128), 16), ((16, 1, 30, 1024), 9),
+     ((16, 1, 200, 2048), 16), ((12, 2, 150, 1024), 12), ((9, 1, 300, 4096), 8),
+     ((9, 2, 700, 2048), 8)],
 )
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 def test_batched_forward_is_at_the_dtype_floor(shape, n_queries, dtype):
