@@ -390,7 +390,8 @@ StreamBwdPlan plan_stream_bwd(int64_t N, int64_t BT, int64_t D, int dtype, const
 // Batched-query register tile: the fp32 tile (N * CPT * VEC floats per thread)
 // must fit kBatchedTileFloats; as many chunks per thread as fit (fewer warps
 // per token: less reduction work per query), groups of up to 256 threads, the
-// queries' S rows in shared memory beside the ring.
+// queries' SB slots (S rounded up to 4, 8 or 16) in shared memory beside the
+// ring.
 TilePlan plan_batched(int64_t N, int64_t BT, int64_t D, int64_t S, int dtype, const DevInfo& di) {
   TilePlan p;
   if (!SY_TUNE_BATCHED_REG) return p;
@@ -416,18 +417,18 @@ TilePlan plan_batched(int64_t N, int64_t BT, int64_t D, int64_t S, int dtype, co
   c.row_chunks = (int)rc;
   c.row_bytes = (int)(D * es);
   c.stats_stride = (int)stats_stride(N);
-  c.red_stride = 32;   // 32-value reductions (query blocks)
-  c.coef_stride = 64;  // alpha as fp32 pairs: up to 32 (query, source) pairs per warp
+  c.red_stride = batched_red_stride((int)N, (int)S);    // the blocks' warp totals
+  c.coef_stride = batched_coef_stride((int)N, (int)S);  // alpha pairs of every query slot
   c.tg = tg;
-  DevInfo room = di;  // the queries take S rows of shared memory
-  room.max_smem = di.max_smem - (int)(S * c.row_bytes) - 128;
+  DevInfo room = di;  // the query slots take SB rows of shared memory
+  room.max_smem = di.max_smem - (int)(batched_slots((int)S) * c.row_bytes) - 128;
   int64_t smem = 0;
   if (room.max_smem <= 0 || !size_ring(c, kOpFwd, kBatchedThreads / tg, room, &smem, true)) return p;
   p.kind = kPlanRegTile;
   p.c = c;
   p.cpt = cpt;
   p.grid = (int)(BT < di.sms ? BT : di.sms);
-  p.smem = (int64_t)(batched_q_off(c) + (size_t)S * c.row_bytes);
+  p.smem = (int64_t)(batched_q_off(c) + (size_t)batched_slots((int)S) * c.row_bytes);
   return p;
 }
 
