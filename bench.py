@@ -597,7 +597,7 @@ def host_cost(dev, calls=400):
     return res
 
 
-def e2e_times(dev, steps, n, b, t, d, op):
+def e2e_times(dev, steps, n, b, t, d, op, pipe_steps=30):
     """The step through the public API from pinned host buffers, every step:
     H2D of v, w and dout, forward + backward (block_attn_res_triton), and D2H
     of the results out, dv and dw -- all inside the events.
@@ -606,7 +606,9 @@ def e2e_times(dev, steps, n, b, t, d, op):
     other). ``pipelined``: the same K steps with the next step's H2D on a copy
     stream and the previous step's D2H on another, overlapping the compute (two
     device buffer sets; PCIe carries the two directions at once); the time is
-    from before the first H2D to after the last D2H, divided by K."""
+    from before the first H2D to after the last D2H, divided by K = pipe_steps
+    (the first step's H2D and the last step's D2H, which nothing overlaps, are
+    spread over K steps: ~1/K of a step's copy time)."""
     gen = torch.Generator().manual_seed(3)
     v_h = torch.randn(n, b, t, d, generator=gen).to(torch.bfloat16).pin_memory()
     w_h = (torch.randn(d, generator=gen) / math.sqrt(d)).to(torch.bfloat16).pin_memory()
@@ -680,7 +682,7 @@ def e2e_times(dev, steps, n, b, t, d, op):
         return start.elapsed_time(end) / k_steps
 
     pipelined(3)
-    pipe_ms = pipelined(steps)
+    pipe_ms = pipelined(pipe_steps)
     return summarize(ms), pipe_ms, h2d, d2h
 
 
@@ -827,8 +829,9 @@ def run_ours(args):
                     "switchyard.sharding.block_attn_res_sharded") +
                    " (autograd) from pinned host buffers on every rank: H2D of v, w, dout and D2H "
                    "of out, dv, dw every step (bytes per rank); value: the next step's H2D and the "
-                   "previous step's D2H overlap the compute on two copy streams (serial_*: one "
-                   "step at a time); max over ranks",
+                   "previous step's D2H overlap the compute on two copy streams, 30 steps "
+                   "from the first H2D to the last D2H (serial_*: one step at a time, 10 "
+                   "steps); max over ranks",
         }
     result = None
     if rank == 0:
