@@ -1,4 +1,4 @@
-"""Benchmark of the Block AttnRes operator on B200.
+"""Benchmark of the Block AttnRes operator on B200 at its representative shape.
 
 Workload (one "step"): forward + backward of ``block_attn_res_triton`` at
 N=9, B=1, T=4096, D=2048 bf16 with v ~ N(0,1), w ~ N(0,1/D), dout ~ N(0,1)
@@ -80,13 +80,13 @@ def parse_args():
     ap.add_argument("--shape", default=None,
                     help="N,B,T,D for --profile (default: the representative shape)")
     ap.add_argument("--decoder", action="store_true",
-                    help="no bench line: the 1.3B Block AttnRes decoder (BASELINE config 5), a bf16 "
+                    help="no bench line: the 1.3B Block AttnRes decoder, a bf16 "
                          "AdamW training step of the standard and the switchyard residual at B=4 "
                          "T=2048 per GPU, DDP over NCCL under torchrun; one JSON line")
     ap.add_argument("--decoder-batch", type=int, default=4)
     ap.add_argument("--decoder-seq", type=int, default=2048)
     ap.add_argument("--grid", action="store_true",
-                    help="no bench line: BASELINE config 4, the shape grid N x B x T x D in bf16 with "
+                    help="no bench line: the benchmark shape grid N x B x T x D in bf16 with "
                          "the token axis sharded over the torchrun world; fwd and fwd+bwd per shape, "
                          "checked against a float64 evaluation; one JSON line per shape")
     ap.add_argument("--grid-max-shapes", type=int, default=0,
@@ -347,7 +347,7 @@ def cpu_baseline(seconds: float):
     """The reference's eager CPU path (restated in oracle/eager_port.py) on the
     bench's own workload, N=9 B=1 T=4096 D=2048 bf16, forward + backward, on
     all host threads; beside it the same in fp32, the forward alone, and
-    BASELINE config 1 (N=4 B=1 T=256 D=512 fp32)."""
+    the small fp32 case N=4 B=1 T=256 D=512."""
     torch.set_num_threads(os.cpu_count() or 1)
     n, b, t, d = REP
     per, reps = cpu_time(n, b, t, d, torch.bfloat16, seconds)
@@ -1141,7 +1141,7 @@ def bf16_floor(want) -> float:
 
 
 def run_grid(args):
-    """N in GRID_N, B in GRID_B, T in GRID_T, D in GRID_D,
+    """The shape grid: N in GRID_N, B in GRID_B, T in GRID_T, D in GRID_D,
     bf16, v ~ N(0,1), w ~ N(0, 1/D), dout ~ N(0,1), each rank generating its
     own contiguous token shard (seed 1000 + rank; w shared). Shapes whose
     per-GPU footprint (v, dv, dout, out, statistics, partial rows) does not fit
@@ -1257,7 +1257,7 @@ def run_grid(args):
 
 
 def run_decoder(args):
-    """the 1.3B decoder (switchyard.decoder, 24 layers, hidden
+    """The 1.3B decoder (switchyard.decoder, 24 layers, hidden
     2048, 16 heads, SwiGLU 5632, 8 blocks, vocabulary 32000, N(0, 0.02) init)
     trained in bf16 with AdamW on synthetic tokens uniform over the vocabulary,
     B x T tokens per GPU, for the standard residual and for Block AttnRes on

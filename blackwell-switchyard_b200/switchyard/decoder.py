@@ -73,7 +73,7 @@ SOURCE_MODES = ("arena", "stack")
 class DecoderConfig:
     """Shape and structure (the reference's ``ModelConfig``, ``model.py:150-202``).
 
-    The defaults are BASELINE config 5, the 1.3 B model: 24 layers, hidden
+    The defaults are the 1.3 B benchmark model: 24 layers, hidden
     2048, 16 heads, SwiGLU 5632, 8 blocks, vocabulary 32000 (the reference's
     own default is 32768).
     """

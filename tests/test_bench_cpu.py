@@ -1,6 +1,6 @@
 """The benchmark's own checkers and bookkeeping, on the CPU.
 
-``bench.py --grid`` checks every shape of BASELINE config 4 with a float64
+``bench.py --grid`` checks every shape of the benchmark grid with a float64
 evaluation on the GPU (``f64_tokens`` / ``f64_dw``); here those functions are
 pinned to the oracle, and the byte model and the summary statistics to their
 definitions.

@@ -98,7 +98,7 @@ def test_parameter_counts_match_the_paper():
 
 
 def test_the_1_3b_configuration():
-    """24 layers, hidden 2048, 16 heads, SwiGLU 5632, 8
+    """The 1.3 B benchmark model: 24 layers, hidden 2048, 16 heads, SwiGLU 5632, 8
     blocks, vocabulary 32000 -- about 1.3 B parameters with tied embeddings."""
     from switchyard.decoder import Decoder, DecoderConfig
 

@@ -1,7 +1,7 @@
 """Behaviour of the drop-in operator on the GPU: the reference's semantic and
 rejection tests (tests/test_triton_op.py:210-288), dispatch pins, edge cases,
 bit-stability, the model-arena calling pattern, and full-size property checks
-at the BASELINE representative shape."""
+at the representative shape (N=9 B=1 T=4096 D=2048 bf16)."""
 
 from __future__ import annotations
 
@@ -338,7 +338,7 @@ def test_bit_stable_across_runs(shape):
 
 
 def test_representative_shape_full_size_properties():
-    """BASELINE config 2 (N=9 B=1 T=4096 D=2048 bf16, v~N(0,1), w~N(0,1/D),
+    """The representative shape (N=9 B=1 T=4096 D=2048 bf16, v~N(0,1), w~N(0,1/D),
     dout~N(0,1)). Tokens are independent, so out and dv are checked exactly
     against the oracle on a sample of tokens; dw (a sum over every token) is
     checked against a chunked float64 sum over all of them."""

@@ -27,7 +27,7 @@ def _close(got, want, rtol=1e-10, atol=1e-12, msg=""):
 
 def test_golden_fixtures_present():
     assert len(CASES) >= 10
-    assert "c1_4_1_256_512" in CASES
+    assert "c1_4_1_256_512" in CASES  # the small fp32 case N=4 T=256 D=512
 
 
 @pytest.mark.parametrize("name", CASES)
