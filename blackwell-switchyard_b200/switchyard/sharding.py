@@ -92,7 +92,7 @@ class PeerExchange:
     queues work ahead of the GPU, so a timeout is seen by a later call, and at
     the latest after the next synchronisation -- and then raises
     :class:`PeerExchangeError`; the exchange stays broken, so no later call can
-    rewrite a slot a late peer may still read.
+    reuse a slot that a late peer may still be writing into.
     """
 
     def __init__(self, group, length: int, device: torch.device):
@@ -147,10 +147,13 @@ class PeerExchange:
 
     def read_timing(self) -> dict:
         """Counters since :meth:`start_timing` (synchronises), per call of the
-        kernel's first block: mean and largest wait from this rank's
-        announcement to the last peer's flag; mean time from the kernel's start
-        to the end of its sum, and of its phases (partial-row sum, slot store
-        and announcement, peer reads and output store)."""
+        kernel's first block: mean and largest wait from the end of this
+        rank's stores into its peers' buffers until every peer's word of this
+        call has arrived in its own; mean time from the kernel's start to the
+        end of its sum, and of its phases: the partial-row sum
+        (``reduce_mean_us``), the tagged stores into the peers' buffers
+        (``announce_mean_us``), and the rank-order sum with the output store
+        (``peer_sum_mean_us``)."""
         c = [int(x) for x in self.timing.tolist()]
         k = max(c[0], 1)
         return {"calls": c[0], "wait_mean_us": c[1] / k / 1e3, "wait_max_us": c[2] / 1e3,
