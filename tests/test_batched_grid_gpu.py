@@ -9,7 +9,8 @@ block's spare lanes or in a block of their own. Each combination below lands on
 a different one of those layouts (and D = 1024 gives 4, 2 and 1 chunks per
 thread as N grows); T = 37 leaves most CTAs with one token and some with none.
 Outputs are checked at the dtype's rounding floor as in ``test_parity_gpu``;
-with statistics (``attn_with_stats``) the (m, l) pairs too.
+with statistics (``attn_with_stats``) the (m, l) pairs too; and the batched
+backward's dv and dq at every N up to 12.
 """
 
 from __future__ import annotations
@@ -83,3 +84,28 @@ def test_statistics_for_every_source_count(n, s):
     check(o, o_w, torch.bfloat16, f"o N={n} S={s}")
     np.testing.assert_allclose(np64(m), m_w, rtol=2e-5, atol=2e-5)
     np.testing.assert_allclose(np64(ell), l_w, rtol=2e-5, atol=2e-5)
+
+
+@pytest.mark.parametrize("s", [1, 2, 5, 8, 16])
+@pytest.mark.parametrize("n", list(range(1, 13)))
+def test_batched_backward_for_every_source_count(n, s):
+    """block_attn_res_batched_train's dv and dq: the register-tile backward for
+    N <= 9 (one CTA per token, every dot product of a token in one pass), the
+    generic kernel beyond."""
+    from switchyard import block_attn_res_batched_train
+
+    dd = 512
+    g = torch.Generator().manual_seed(400 * n + s)
+    v = torch.randn(n, 1, T, dd, generator=g).to(torch.bfloat16).to(DEV)
+    q = torch.randn(s, dd, generator=g)
+    q = (q / q.norm(dim=-1, keepdim=True) * 4.0).to(torch.bfloat16).to(DEV)
+    gout = torch.randn(s, 1, T, dd, generator=g).to(torch.bfloat16).to(DEV)
+    vt = v.clone().requires_grad_(True)
+    qt = q.clone().requires_grad_(True)
+    block_attn_res_batched_train(vt, qt, DEFAULT_EPS).backward(gout)
+    dv_w, dq_w = O.batched_backward(np64(v), np64(q), np64(gout), DEFAULT_EPS)
+    check(vt.grad, dv_w, torch.bfloat16, f"dv N={n} S={s}")
+    if n == 1:  # one source: the softmax is identically 1 and dq exactly zero
+        assert qt.grad.abs().max().item() == 0.0
+    else:
+        check(qt.grad, dq_w, torch.bfloat16, f"dq N={n} S={s}")
