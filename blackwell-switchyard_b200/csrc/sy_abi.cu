@@ -797,8 +797,8 @@ int64_t sy_bwd_batched_partials(int64_t N, int64_t BT, int64_t D, int64_t S, int
   if (BT == 0 || D == 0) return 1;
   DevInfo di;
   if (dev_info(&di) != cudaSuccess) return -SY_ERR_CUDA;
-  // register tile: as many CTAs per SM as its registers and shared memory
-  // (its dq columns) allow, one or two; generic: two per SM
+  // register tile: one CTA per SM for the staged kernel, one or two for the
+  // half-pass kernel as its shared memory (its dq columns) allows; generic: two
   const int rc = reg_bwd_batched_ctas_per_sm((int)N, (int)D, (int)S, dtype, di.max_smem);
   const int64_t g = (int64_t)di.sms * (rc > 0 ? rc : 2);
   return BT < g ? BT : g;
@@ -822,10 +822,10 @@ int sy_bwd_batched(const void* v, const void* queries, const void* g, void* dv,
   DevInfo di;
   cudaError_t e = dev_info(&di);
   if (e != cudaSuccess) return cuda_status(e, "sy_bwd_batched: device query");
-  const int ctas = reg_bwd_batched_ctas_per_sm((int)N, (int)D, (int)S, dtype, di.max_smem);
-  if (ctas > 0 && al16(v) && al16(queries) && al16(g) && al16(dv) && al16(dq_partial)) {
+  const int variant = reg_bwd_batched_variant((int)N, (int)D, (int)S, dtype, di.max_smem);
+  if (variant > 0 && al16(v) && al16(queries) && al16(g) && al16(dv) && al16(dq_partial)) {
     e = launch_reg_bwd_batched(BT, (int)N, (int)D, (int)S, dtype, v, queries, g, dv, dq_partial,
-                               (int)P, eps, ctas, st);
+                               (int)P, eps, variant, st);
     return cuda_status(e, "sy_bwd_batched: register-tile kernel launch");
   }
   if (bwd_batched_smem((int)N, (int)S) > (size_t)di.max_smem) return SY_ERR_UNSUPPORTED;

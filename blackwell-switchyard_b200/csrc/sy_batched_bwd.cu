@@ -187,6 +187,10 @@ __global__ void __launch_bounds__(kGenericThreads)
 //     written once as the CTA's partial row.
 // ---------------------------------------------------------------------------
 constexpr int kBwdRegMaxN = 9;
+constexpr int kRegBwdStaged = 3;  // reg_bwd_batched_variant: the staged kernel
+#ifndef SY_TUNE_BWD_STAGED_MIN_S
+#define SY_TUNE_BWD_STAGED_MIN_S 1  // smallest S the staged kernel takes
+#endif
 int reg_bwd_batched_ctas_per_sm(int N, int D, int S, int dtype, int max_smem);  // no spills for any dtype up to here (fp16 spills from 10)
 
 template <typename T>
@@ -376,12 +380,216 @@ __global__ void __launch_bounds__(kGenericThreads, MINB)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Staged variant (S <= 8 at 4 KiB rows; one CTA of 8 warps per SM): the
+// token's N source chunks unpacked to fp32 once (N x VEC floats a thread, so
+// every dot product and dv term comes from registers and dv is one pass over
+// the queries), the next token's source chunks requested into registers and
+// its g chunks copied into shared memory (cp.async, two buffers) at the start
+// of this token, so neither waits on HBM. A thread copies and reads only its
+// own chunk positions, so the copies need no barrier: it waits for its own
+// previous copy group. The numbers are the same as the half-pass kernel's
+// (same per-element operation order), except for the dq partial-row count.
+// ---------------------------------------------------------------------------
+__host__ __device__ inline size_t reg_bwd_staged_g_off(int N, int S, int rc, int vec) {
+  return (reg_bwd_batched_layout(N, S, rc, vec).total + 15) / 16 * 16;
+}
+__host__ __device__ inline size_t reg_bwd_staged_total(int N, int S, int rc, int vec) {
+  return reg_bwd_staged_g_off(N, S, rc, vec) + (size_t)2 * S * rc * 16;  // [2][S][rc] uint4
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+// All but the most recent of this thread's copy groups have landed.
+__device__ __forceinline__ void cp_async_wait_prev() {
+  asm volatile("cp.async.wait_group 1;" ::: "memory");
+}
+
+// The packed dot product of two unpacked chunks: even and odd elements in the
+// two lanes of one fp32 pair, added once (the same order as dot_chunk).
+template <int P>
+__device__ __forceinline__ float dot_pairs(const float2 (&a)[P], const float2 (&b)[P]) {
+  float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < P; ++i) acc = __ffma2_rn(a[i], b[i], acc);
+  return acc.x + acc.y;
+}
+
+template <typename T, int N>
+__global__ void __launch_bounds__(kGenericThreads, 1)
+    reg_bat_bwd_staged_kernel(const T* __restrict__ v, const T* __restrict__ q,
+                              const T* __restrict__ g, T* __restrict__ dv,
+                              float* __restrict__ dq_partial, long long BT, int D, int S, int rc,
+                              float eps) {
+  constexpr int VEC = Dt<T>::kVec;
+  constexpr int P = VEC / 2;
+  extern __shared__ __align__(16) unsigned char rsm[];
+  const RegBwdSmem L = reg_bwd_batched_layout(N, S, rc, VEC);
+  uint4* qs = reinterpret_cast<uint4*>(rsm + L.q_off);
+  float* dqs = reinterpret_cast<float*>(rsm + L.dq_off);
+  float* red = reinterpret_cast<float*>(rsm + L.red_off);
+  float2* coef = reinterpret_cast<float2*>(rsm + L.coef_off);
+  float* cvp = reinterpret_cast<float*>(rsm + L.cvp_off);
+  uint4* gbuf = reinterpret_cast<uint4*>(rsm + reg_bwd_staged_g_off(N, S, rc, VEC));
+  const int tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+  const bool act = tid < rc;
+  const uint4 z4 = make_uint4(0u, 0u, 0u, 0u);
+  for (int i = tid; i < S * rc; i += kGenericThreads)
+    qs[i] = reinterpret_cast<const uint4*>(q)[i];
+  for (int i = tid; i < S * rc * VEC; i += kGenericThreads) dqs[i] = 0.f;
+  __syncthreads();
+  const float inv_d = 1.f / (float)D;
+  const size_t gstride = (size_t)BT * D / VEC;  // one query's slab of g, in chunks
+  // this thread's chunk of every query's g row of token `tk`, into buffer `bi`;
+  // every thread commits a group (an empty one when it copies nothing)
+  auto stage_g = [&](long long tk, int bi) {
+    if (act && tk < BT) {
+      const uint4* src = reinterpret_cast<const uint4*>(g + (size_t)tk * D) + tid;
+      uint4* dst = gbuf + (size_t)bi * S * rc + tid;
+      for (int s = 0; s < S; ++s) cp_async16(dst + (size_t)s * rc, src + (size_t)s * gstride);
+    }
+    cp_async_commit();
+  };
+  uint4 vn[N];  // the raw source chunks of the next token
+#pragma unroll
+  for (int n = 0; n < N; ++n)
+    vn[n] = act && (long long)blockIdx.x < BT
+                ? reinterpret_cast<const uint4*>(v + ((size_t)n * BT + blockIdx.x) * D)[tid]
+                : z4;
+  stage_g(blockIdx.x, 0);
+  int j = 0;
+  for (long long tok = blockIdx.x; tok < BT; tok += gridDim.x, ++j) {
+    float2 vf[N][P];
+#pragma unroll
+    for (int n = 0; n < N; ++n) unpack2<T>(vn[n], vf[n]);
+    const long long nxt = tok + gridDim.x;
+#pragma unroll
+    for (int n = 0; n < N; ++n)
+      vn[n] = act && nxt < BT
+                  ? reinterpret_cast<const uint4*>(v + ((size_t)n * BT + nxt) * D)[tid]
+                  : z4;
+    stage_g(nxt, (j + 1) & 1);
+    cp_async_wait_prev();  // this token's g chunks have landed
+    const uint4* gtok = gbuf + (size_t)(j & 1) * S * rc + tid;
+    {
+      float sv[16];
+#pragma unroll
+      for (int n = 0; n < 16; ++n) sv[n] = n < N ? dot_pairs<P>(vf[n], vf[n]) : 0.f;
+      const float t = warp_reduce_scatter16(sv, lane);
+      if ((lane & 1) == 0 && (lane >> 1) < N) red[((size_t)S * kBW + wp) * 32 + (lane >> 1)] = t;
+    }
+    for (int s = 0; s < S; ++s) {
+      const uint4 gx = act ? gtok[(size_t)s * rc] : z4;
+      const uint4 qx = act ? qs[s * rc + tid] : z4;
+      float2 gf[P], qf[P];
+      unpack2<T>(gx, gf);
+      unpack2<T>(qx, qf);
+      float a[32];
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        a[n] = n < N ? dot_pairs<P>(qf, vf[n]) : 0.f;
+        a[16 + n] = n < N ? dot_pairs<P>(gf, vf[n]) : 0.f;
+      }
+      const float t = warp_reduce_scatter<32>(a, lane);
+      if ((lane & 15) < N) red[((size_t)s * kBW + wp) * 32 + lane] = t;
+    }
+    __syncthreads();
+    for (int s = wp; s < S; s += kBW) {
+      const bool on = lane < N;
+      const int n = on ? lane : 0;
+      float a = 0.f, G = 0.f, ssq = 0.f;
+      for (int k = 0; k < kBW; ++k) {
+        a += red[((size_t)s * kBW + k) * 32 + n];
+        G += red[((size_t)s * kBW + k) * 32 + 16 + n];
+        ssq += red[((size_t)S * kBW + k) * 32 + n];
+      }
+      const float r = rsqrtf(ssq * inv_d + eps);
+      const float lg = a * r;
+      const float m = warp_max(on ? lg : -INFINITY);
+      const float e = on ? expf(lg - m) : 0.f;
+      const float al = e / warp_sum(e);
+      const float delta = warp_sum(on ? al * G : 0.f);
+      const float dl = al * (G - delta);
+      if (on) {
+        coef[s * N + n] = make_float2(al, dl * r);
+        cvp[s * N + n] = -dl * lg * r * r * inv_d;
+      }
+    }
+    __syncthreads();
+    float2 acc[N][P];
+    float cvn[N];
+#pragma unroll
+    for (int n = 0; n < N; ++n) {
+      cvn[n] = 0.f;
+#pragma unroll
+      for (int i = 0; i < P; ++i) acc[n][i] = make_float2(0.f, 0.f);
+    }
+    for (int s = 0; s < S; ++s) {
+      const uint4 gx = act ? gtok[(size_t)s * rc] : z4;
+      const uint4 qx = act ? qs[s * rc + tid] : z4;
+      float2 gf[P], qf[P], dqp[P];
+      unpack2<T>(gx, gf);
+      unpack2<T>(qx, qf);
+#pragma unroll
+      for (int i = 0; i < P; ++i) dqp[i] = make_float2(0.f, 0.f);
+#pragma unroll
+      for (int n = 0; n < N; ++n) {
+        const float2 cf = coef[s * N + n];
+        cvn[n] += cvp[s * N + n];
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+          acc[n][i] = __ffma2_rn(f2(cf.x), gf[i], acc[n][i]);
+          acc[n][i] = __ffma2_rn(f2(cf.y), qf[i], acc[n][i]);
+          dqp[i] = __ffma2_rn(f2(cf.y), vf[n][i], dqp[i]);
+        }
+      }
+      if (act) {
+        float2* dq2 = reinterpret_cast<float2*>(dqs + (size_t)s * rc * VEC + (size_t)tid * VEC);
+#pragma unroll
+        for (int i = 0; i < P; ++i) {
+          const float2 o = dq2[i];
+          dq2[i] = make_float2(o.x + dqp[i].x, o.y + dqp[i].y);
+        }
+      }
+    }
+    if (act) {
+#pragma unroll
+      for (int n = 0; n < N; ++n) {
+        float2 o[P];
+#pragma unroll
+        for (int i = 0; i < P; ++i) o[i] = __ffma2_rn(f2(cvn[n]), vf[n][i], acc[n][i]);
+        reinterpret_cast<uint4*>(dv + ((size_t)n * BT + tok) * D)[tid] = pack2<T>(o);
+      }
+    }
+  }
+  if (act) {
+    float* prow = dq_partial + (size_t)blockIdx.x * S * D;
+    for (int s = 0; s < S; ++s) {
+      const float4* src =
+          reinterpret_cast<const float4*>(dqs + (size_t)s * rc * VEC + (size_t)tid * VEC);
+      float4* dst = reinterpret_cast<float4*>(prow + (size_t)s * D + (size_t)tid * VEC);
+#pragma unroll
+      for (int i = 0; i < VEC / 4; ++i) dst[i] = src[i];
+    }
+  }
+}
+
 template <typename T, int N>
 static cudaError_t launch_reg_bat_bwd_n(long long BT, int D, int S, int rc, const void* v,
                                         const void* q, const void* g, void* dv, float* dqp, int P,
-                                        float eps, int ctas, cudaStream_t st) {
+                                        float eps, int variant, cudaStream_t st) {
+  if (variant == kRegBwdStaged)
+    return launch_smem(reg_bat_bwd_staged_kernel<T, N>, P, kGenericThreads,
+                       reg_bwd_staged_total(N, S, rc, Dt<T>::kVec), st, static_cast<const T*>(v),
+                       static_cast<const T*>(q), static_cast<const T*>(g), static_cast<T*>(dv),
+                       dqp, BT, D, S, rc, eps);
   const size_t smem = reg_bwd_batched_layout(N, S, rc, Dt<T>::kVec).total;
-  if (ctas == 2)
+  if (variant == 2)
     return launch_smem(reg_bat_bwd_kernel<T, N, 2>, P, kGenericThreads, smem, st,
                        static_cast<const T*>(v), static_cast<const T*>(q), static_cast<const T*>(g),
                        static_cast<T*>(dv), dqp, BT, D, S, rc, eps);
@@ -393,11 +601,11 @@ static cudaError_t launch_reg_bat_bwd_n(long long BT, int D, int S, int rc, cons
 template <typename T>
 static cudaError_t launch_reg_bat_bwd_t(int N, long long BT, int D, int S, int rc, const void* v,
                                         const void* q, const void* g, void* dv, float* dqp, int P,
-                                        float eps, int ctas, cudaStream_t st) {
+                                        float eps, int variant, cudaStream_t st) {
   switch (N) {
 #define SY_RB_CASE(k) \
   case k:             \
-    return launch_reg_bat_bwd_n<T, k>(BT, D, S, rc, v, q, g, dv, dqp, P, eps, ctas, st);
+    return launch_reg_bat_bwd_n<T, k>(BT, D, S, rc, v, q, g, dv, dqp, P, eps, variant, st);
     SY_RB_CASE(1) SY_RB_CASE(2) SY_RB_CASE(3) SY_RB_CASE(4) SY_RB_CASE(5) SY_RB_CASE(6)
     SY_RB_CASE(7) SY_RB_CASE(8) SY_RB_CASE(9)
 #undef SY_RB_CASE
@@ -406,41 +614,49 @@ static cudaError_t launch_reg_bat_bwd_t(int N, long long BT, int D, int S, int r
   }
 }
 
-// Whether the register-tile variant takes a shape: rows of whole 16-byte
-// chunks, at most one chunk per thread, N <= kBwdRegMaxN, S <= 16, and its
-// shared memory within the device's opt-in limit.
-bool reg_bwd_batched_fits(int N, int D, int S, int dtype, int max_smem) {
-  return reg_bwd_batched_ctas_per_sm(N, D, S, dtype, max_smem) > 0;
-}
-
-// CTAs of the register-tile variant resident per SM (its registers allow two;
-// shared memory may allow fewer), 0 when the variant does not take the shape.
-// An SM's shared memory is the per-block opt-in limit plus the 1 KiB the
-// runtime reserves per block.
-int reg_bwd_batched_ctas_per_sm(int N, int D, int S, int dtype, int max_smem) {
+// Which register-tile kernel takes a shape (rows of whole 16-byte chunks, at
+// most one chunk per thread, N <= kBwdRegMaxN, S <= 16): the staged kernel where
+// its shared memory (two buffers of the token's g chunks beside the half-pass
+// kernel's) fits and S >= SY_TUNE_BWD_STAGED_MIN_S, else the half-pass kernel
+// at two CTAs per SM where two fit the SM's shared memory (the per-block
+// opt-in limit plus the 1 KiB the runtime reserves per block), else at one;
+// 0 when none takes it.
+int reg_bwd_batched_variant(int N, int D, int S, int dtype, int max_smem) {
   const int es = dtype == SY_F32 ? 4 : 2;
   if (N < 1 || N > kBwdRegMaxN || S < 1 || S > kBwdBatchedMaxS || (D * es) % 16) return 0;
   const int rc = D * es / 16;
   if (rc > kGenericThreads) return 0;
+  if (S >= SY_TUNE_BWD_STAGED_MIN_S && reg_bwd_staged_total(N, S, rc, 16 / es) <= (size_t)max_smem)
+    return kRegBwdStaged;
   const size_t smem = reg_bwd_batched_layout(N, S, rc, 16 / es).total;
   if (smem > (size_t)max_smem) return 0;
   return 2 * (smem + 1024) <= (size_t)max_smem + 1024 ? 2 : 1;
 }
 
+bool reg_bwd_batched_fits(int N, int D, int S, int dtype, int max_smem) {
+  return reg_bwd_batched_variant(N, D, S, dtype, max_smem) > 0;
+}
+
+// CTAs of the chosen register-tile kernel resident per SM (0: none takes the shape).
+int reg_bwd_batched_ctas_per_sm(int N, int D, int S, int dtype, int max_smem) {
+  const int var = reg_bwd_batched_variant(N, D, S, dtype, max_smem);
+  return var == 2 ? 2 : (var > 0 ? 1 : 0);
+}
+
 cudaError_t launch_reg_bwd_batched(long long BT, int N, int D, int S, int dtype, const void* v,
                                    const void* q, const void* g, void* dv, float* dq_partial,
-                                   int P, float eps, int ctas, cudaStream_t st) {
+                                   int P, float eps, int variant, cudaStream_t st) {
   const int rc = D * (dtype == SY_F32 ? 4 : 2) / 16;
   switch (dtype) {
     case SY_BF16:
       return launch_reg_bat_bwd_t<__nv_bfloat16>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps,
-                                                 ctas, st);
+                                                 variant, st);
     case SY_F16:
-      return launch_reg_bat_bwd_t<__half>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps, ctas,
-                                          st);
+      return launch_reg_bat_bwd_t<__half>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps,
+                                          variant, st);
     case SY_F32:
-      return launch_reg_bat_bwd_t<float>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps, ctas,
-                                         st);
+      return launch_reg_bat_bwd_t<float>(N, BT, D, S, rc, v, q, g, dv, dq_partial, P, eps,
+                                         variant, st);
     default:
       return cudaErrorInvalidValue;
   }

@@ -116,11 +116,12 @@ cudaError_t launch_bwd_batched(long long BT, int N, int D, int S, int dtype, con
 size_t bwd_batched_smem(int N, int S);
 bool reg_bwd_batched_fits(int N, int D, int S, int dtype, int max_smem);
 int reg_bwd_batched_ctas_per_sm(int N, int D, int S, int dtype, int max_smem);
+int reg_bwd_batched_variant(int N, int D, int S, int dtype, int max_smem);
 cudaError_t launch_stage(long long numel, int dtype, const void* partial, const void* out,
                          void* new_partial, void* arena, bool vec16, int grid, cudaStream_t st);
 cudaError_t launch_reg_bwd_batched(long long BT, int N, int D, int S, int dtype, const void* v,
                                    const void* q, const void* g, void* dv, float* dq_partial,
-                                   int P, float eps, int ctas, cudaStream_t st);
+                                   int P, float eps, int variant, cudaStream_t st);
 cudaError_t launch_merge(long long R, int D, int dtype, const void* o1, const float* ms1,
                          const void* o2, const float* ms2, void* o, float* ms, int normalize,
                          int vec16, int grid, cudaStream_t st);
