@@ -239,3 +239,21 @@ def test_torch_extension_loads_over_the_same_library():
     maps = open("/proc/self/maps").read()
     mapped = {line.split()[-1] for line in maps.splitlines() if "libswitchyard_b200.so" in line}
     assert mapped == {str(_native.LIB_PATH.resolve())}, mapped
+
+
+def test_batched_planner_sizes_query_slots(native):
+    """The register-tile batched forward is compiled for 4, 8 or 16 query slots
+    (S rounded up, the extra slots zero rows): its plan depends only on the
+    slot count, every plan fits the opt-in shared memory with at least a stage
+    per group, and the slot rows take shared memory from the ring."""
+    import torch
+
+    plans = {s: native.plan_info(2, 9, 4096, 2048, s, torch.bfloat16, **B200)
+             for s in (2, 3, 4, 5, 8, 9, 12, 16)}
+    for a, b in ((2, 4), (3, 4), (5, 8), (9, 16), (12, 16)):
+        assert plans[a] == plans[b], (a, b)
+    for p in plans.values():
+        assert p["kind"] == 1 and p["stages"] >= p["groups"]
+        assert p["smem_bytes"] <= B200["max_smem"]
+    assert plans[4]["smem_bytes"] < plans[8]["smem_bytes"]
+    assert plans[16]["stages"] < plans[8]["stages"]
